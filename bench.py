@@ -1,0 +1,365 @@
+"""Benchmark of the routed-expert MoE layer at decode on B200.
+
+Default: N=1, one MoE layer of 288 routed experts + 1 shared expert, H=6144, I=1536, K=3 trellis, B=64 decode tokens,
+uniform top-8 sigmoid routing (fresh routing per step from a pool of 16 seeded routings), fp16 activations.
+A step = one glmx_moe_forward (split -> gate/up dequant-GEMV -> down dequant-GEMV -> combine) over B tokens.
+Prints ONE JSON line (rank 0). `--impl reference` times the reference's own CPU implementation (kernels/cpu_avx2
+ft_core.h, built into oracle/_ref/libftref.so) on the host cores instead.
+
+Multi-GPU (torchrun, one rank per GPU): every rank holds its own layer and runs B tokens per step (replicas of the
+single-GPU workload, weak scaling); time = max over ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "glm-flash-lite_b200"))
+
+H, I, E, TOPK = 6144, 1536, 288, 8
+EXPERT_BYTES_K3 = 3 * (H // 16) * (I // 16) * 96          # 10,616,832 trellis bytes per expert
+SCALE_BYTES = 3 * (H + I) * 2                              # suh + svh fp16 of gate, up, down: 46,080
+ROUTE_POOL = 16
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.stop_ev = threading.Event()
+        self.th = threading.Thread(target=self.run, daemon=True)
+
+    def run(self):
+        while not self.stop_ev.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self.stop_ev.wait(0.2)
+
+    def __enter__(self):
+        self.th.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        self.th.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[4:8]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def make_routes(B, seed):
+    from glmx import synth
+    return [synth.route_uniform(B, E, TOPK, seed + i) for i in range(ROUTE_POOL)]
+
+
+def unique_touched(routes):
+    return [int(np.unique(s).size) for s, _ in routes]
+
+
+# ------------------------------------------------------------------------------------------------------------------
+def cpu_reference_run(B: int, seconds: float, threads: int, seed: int = 0):
+    """The reference's moe_forward (EXACT mode, ft_core.h:1338-1407) at BASELINE geometry on the host cores, with
+    the shared expert folded in as an extra pick of weight 1. Returns (tok/s, calls, seconds, threads)."""
+    from glmx import synth
+    from oracle import oracle as O
+    ref = O.Reference()
+    bank = synth.make_bank(H, I, E, shared=True, seed=seed)
+    layer = ref.layer(bank, with_shared=True)
+    cpus = sorted(os.sched_getaffinity(0))
+    ref.start_pool(threads, cpus[:threads] if len(cpus) >= threads else cpus)
+    routes = make_routes(B, 1000 + seed)
+    x = synth.make_x(B, H, 7).astype(np.float32)
+    prepared = [O.with_shared_routes(s, w, E) for s, w in routes]
+    ref.moe_forward(layer, x, *prepared[0], mode=1)          # warm
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        ref.moe_forward(layer, x, *prepared[calls % len(prepared)], mode=1)
+        calls += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds and calls >= 2:
+            break
+    ref.stop_pool()
+    return B * calls / dt, calls, dt
+
+
+def cpu_threads():
+    try:
+        from oracle.oracle import REF_SO  # noqa: F401
+    except Exception:
+        pass
+    n = len(os.sched_getaffinity(0))
+    return max(1, n - 2) if n > 3 else n
+
+
+def run_reference_impl(args, rank, world):
+    """`--impl reference`: the reference CPU tier timed on this host (rank 0 only)."""
+    if rank != 0:
+        return
+    from oracle.oracle import REF_SO
+    if not os.path.exists(REF_SO):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libftref.so was not built (needs the reference tree at build time)"}))
+        return
+    threads = cpu_threads()
+    per_step = []
+    from glmx import synth
+    from oracle import oracle as O
+    ref = O.Reference()
+    bank = synth.make_bank(H, I, E, shared=True, seed=0)
+    layer = ref.layer(bank, with_shared=True)
+    cpus = sorted(os.sched_getaffinity(0))
+    ref.start_pool(threads, cpus[:threads])
+    routes = [O.with_shared_routes(s, w, E) for s, w in make_routes(args.batch, 1000)]
+    x = synth.make_x(args.batch, H, 7).astype(np.float32)
+    for i in range(args.warmup):
+        ref.moe_forward(layer, x, *routes[i % len(routes)], mode=1)
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        ref.moe_forward(layer, x, *routes[i % len(routes)], mode=1)
+        per_step.append(time.perf_counter() - t0)
+    ref.stop_pool()
+    T = sum(per_step)
+    v = args.batch * args.steps / T
+    print(json.dumps({
+        "impl": "reference", "metric": "moe_layer_decode_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32-acc/fp16-weights", "data": "synthetic",
+        "config": {"workload": f"configs[1] decode MoE layer B={args.batch}", "H": H, "I": I, "experts": E, "shared": 1,
+                   "bits": 3, "topk": TOPK, "batch": args.batch, "mode": "EXACT"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} full B={args.batch} layer calls of ft_core.h moe_forward (EXACT)"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", default="1,8,32", help="extra decode batches measured (device time only)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference_impl(args, rank, world)
+
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from glmx import MoELayer
+    from glmx import _lib
+
+    # ---- synthetic layer on the device: 289 experts x (gate|up|down) K=3 trellis + scales ----
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    et = E + 1
+    bank = torch.randint(0, 256, (et * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
+    base = bank.data_ptr()
+    proj = (H // 16) * (I // 16) * 96
+    ptrs = torch.tensor([[base + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(et)], dtype=torch.int64)
+    def sign(shape):
+        return torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
+    suh = [sign((et, k)).half() for k in (H, H, I)]
+    svh = [(sign((et, n)) * (0.02 + 0.005 * torch.randn((et, n), device=dev, generator=g)).abs()).half() for n in (I, I, H)]
+    layer = MoELayer(H, I, E, ptrs, suh, svh, bits=(3, 3, 3), has_shared=True, keep=[bank], device=dev)
+    stream = torch.cuda.current_stream(dev)
+    pk, pk_kind = peaks()
+
+    def device_run(B, steps, warmup, flush_l2=False):
+        routes = make_routes(B, 1000 + 97 * rank)
+        sel = [torch.from_numpy(s).to(dev) for s, _ in routes]
+        wts = [torch.from_numpy(w).to(dev) for _, w in routes]
+        x = (torch.randn((B, H), device=dev, generator=g)).half()
+        out = torch.empty((B, H), dtype=torch.float32, device=dev)
+        uniq = unique_touched(routes)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_l2 else None
+        ph = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.PHASES)] for _ in range(steps)]
+        for i in range(warmup):
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+        gap = 0.0
+        t0.record(stream)
+        for i in range(steps):
+            if flush is not None:
+                flush.zero_()
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, events=ph[i])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        total_ms = t0.elapsed_time(t1)
+        step_ms = [ph[i][0].elapsed_time(ph[i][5]) for i in range(steps)]
+        phase_ms = [[ph[i][k].elapsed_time(ph[i][k + 1]) for k in range(_lib.PHASES - 1)] for i in range(steps)]
+        flags = layer.check_device(B, TOPK)
+        if flags:
+            raise RuntimeError(f"device error flags {flags}")
+        return dict(total_ms=total_ms, step_ms=step_ms, phase_ms=phase_ms, uniq=uniq, gap=gap,
+                    flushed=flush is not None)
+
+    def step_bytes(uniq_list, steps):
+        """algorithmic bytes of one step: every touched expert (+ shared) once: trellis + scales; activations."""
+        u = [uniq_list[i % ROUTE_POOL] + 1 for i in range(steps)]
+        return [n * (EXPERT_BYTES_K3 + SCALE_BYTES) for n in u], [n * 2 * proj for n in u]
+
+    # ---- headline: B = args.batch, inputs > L2 at B=64 (240 experts ~ 2.6 GB per step) ----
+    B = args.batch
+    clk_idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    with ClockSampler(clk_idx) as cs:
+        r = device_run(B, args.steps, args.warmup, flush_l2=B < 32)
+    clocks = cs.summary()
+    T_ms = r["total_ms"]
+    if dist:
+        t = torch.tensor([T_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        T_ms = float(t.item())
+    value = world * B * args.steps / (T_ms / 1e3)
+    lay_bytes, gu_bytes = step_bytes(r["uniq"], args.steps)
+    gu_ms = [p[2] for p in r["phase_ms"]]
+    step_ms = r["step_ms"]
+    achieved_layer_gbs = sum(lay_bytes) / (sum(step_ms) / 1e3) / 1e9
+    gu_gbs = sum(gu_bytes) / (sum(gu_ms) / 1e3) / 1e9
+    phase_share = [sum(p[k] for p in r["phase_ms"]) / sum(step_ms) for k in range(_lib.PHASES - 1)]
+
+    # ---- end to end through the public API: pinned host inputs, H2D, forward, D2H of the result ----
+    routes = make_routes(B, 5000 + rank)
+    x_h = torch.randn((B, H)).half().pin_memory()
+    sel_h = [torch.from_numpy(s).pin_memory() for s, _ in routes]
+    w_h = [torch.from_numpy(w).pin_memory() for _, w in routes]
+    out_h = torch.empty((B, H), dtype=torch.float32).pin_memory()
+    x_d = torch.empty((B, H), dtype=torch.float16, device=dev)
+    s_d = torch.empty((B, TOPK), dtype=torch.int32, device=dev)
+    w_d = torch.empty((B, TOPK), dtype=torch.float32, device=dev)
+    o_d = torch.empty((B, H), dtype=torch.float32, device=dev)
+    def e2e_step(i):
+        x_d.copy_(x_h, non_blocking=True); s_d.copy_(sel_h[i % ROUTE_POOL], non_blocking=True)
+        w_d.copy_(w_h[i % ROUTE_POOL], non_blocking=True)
+        layer.forward(x_d, s_d, w_d, out=o_d)
+        out_h.copy_(o_d, non_blocking=True)
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * B * args.steps / (e2e_ms / 1e3)
+    h2d = x_h.numel() * 2 + B * TOPK * 4 * 2
+    d2h = out_h.numel() * 4
+
+    # ---- decode batch sweep (device time) ----
+    sweep = {}
+    for b in [int(v) for v in args.sweep.split(",") if v.strip()]:
+        if b == B:
+            continue
+        rs = device_run(b, max(10, args.steps // 2), 3, flush_l2=b < 32)
+        lb, _ = step_bytes(rs["uniq"], len(rs["step_ms"]))
+        sweep[str(b)] = {"tok_per_s": b * len(rs["step_ms"]) / (sum(rs["step_ms"]) / 1e3),
+                         "ms_per_step": statistics.mean(rs["step_ms"]),
+                         "hbm_gbs": sum(lb) / (sum(rs["step_ms"]) / 1e3) / 1e9,
+                         "unique_experts": statistics.mean(rs["uniq"]), "l2_flushed": rs["flushed"]}
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        try:
+            from oracle.oracle import REF_SO
+            if os.path.exists(REF_SO):
+                thr = cpu_threads()
+                v, calls, dt = cpu_reference_run(B, args.cpu_seconds, thr)
+                cpu = {"value": v, "unit": "tok/s", "cores": thr, "kind": "reference",
+                       "sample": f"{calls} full B={B} layer calls ({dt:.1f} s) of the reference ft_core.h moe_forward, EXACT mode, shared expert as a weight-1 pick"}
+            else:
+                cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+        except Exception as ex:  # the baseline is reported, never the target
+            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": f"failed: {ex!r}"[:200]}
+
+    peak = pk["hbm_gbs"]
+    line = {
+        "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16-weights/fp32-acc", "data": "synthetic",
+        "config": {"workload": f"configs[1] decode MoE layer B={B} (288 routed + 1 shared, H=6144, I=1536, K=3, top-8)",
+                   "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": "EXACT",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (touched trellis per step > 126 MB)" if B >= 32 else "L2 flushed between steps",
+                   "unique_experts_per_step": statistics.mean(r["uniq"])},
+        "hbm_gbs_layer": achieved_layer_gbs,
+        "roofline": {"bound": "hbm", "kernel": "gemv<gate+up>", "achieved": gu_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gu_gbs / peak, "peak_kind": pk_kind, "traffic": None,
+                     "layer_achieved": achieved_layer_gbs, "layer_frac": achieved_layer_gbs / peak},
+        "phase_share": dict(zip(["route", "prep", "gemv_gateup", "gemv_down", "combine"], phase_share)),
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clocks,
+        "sweep": sweep,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

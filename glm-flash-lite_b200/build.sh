@@ -1,0 +1,20 @@
+#!/usr/bin/env bash
+# Builds libglmx.so (sm_100a) in-tree: glm-flash-lite_b200/lib/libglmx.so. Static CUDA runtime, no torch linkage.
+set -euo pipefail
+HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+NVCC="${NVCC:-nvcc}"
+OUT="$HERE/lib"
+OBJ="$HERE/_build"
+mkdir -p "$OUT" "$OBJ"
+FLAGS=(-std=c++17 -O3 -lineinfo -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC -Xcompiler -fvisibility=hidden
+       --expt-relaxed-constexpr -I"$HERE/../include" ${GLMX_NVCC_EXTRA:-})
+SRCS=(route.cu moe_decode.cu capi.cu)
+objs=()
+for s in "${SRCS[@]}"; do
+  o="$OBJ/${s%.cu}.o"
+  "$NVCC" "${FLAGS[@]}" -c "$HERE/csrc/$s" -o "$o"
+  objs+=("$o")
+done
+"$NVCC" -shared -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC "${objs[@]}" -o "$OUT/libglmx.so.tmp"
+mv "$OUT/libglmx.so.tmp" "$OUT/libglmx.so"
+echo "built $OUT/libglmx.so"

@@ -1,0 +1,190 @@
+// Shared device helpers of the routed-expert MoE path (sm_100a).
+//
+// EXL3 "MUL1" trellis tiles (restated from nkeilar/glm-flash-lite kernels/cpu_avx2/ft_core.h:28-83):
+//   a 16x16 tile of K-bit weights is a circular bit stream of 256*K bits stored as little-endian 32-bit words,
+//   most significant bit first inside each word. Weight i's 16-bit state is the window ending at bit i*K+K
+//   (ft_core.h:65-73); its value is fp16(fma(1024 + bytesum(state * 0x83DCD12D), KINV, KBIAS)) (ft_core.h:75-83).
+//   Stream weights 8t..8t+7 sit at the tile positions the mma.m16n8k16 A fragment gives lane t when A = W^T
+//   (PERM, ft_core.h:48-61), so one lane decodes exactly its own fragment.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace glmx {
+
+constexpr uint32_t MUL1 = 0x83DCD12Du;
+constexpr float HAD = 0.088388347648f;          // 1/sqrt(128) as the reference writes it (ft_core.h:29)
+constexpr uint16_t KINV_BITS = 0x1eee;          // ft_core.h:38
+constexpr uint16_t KBIAS_BITS = 0xc931;         // ft_core.h:39
+constexpr int MAXM = 8;                         // tokens per job (ft_core.h:32)
+constexpr int WAIT_TIMEOUT_NS = 2000000000;     // bounded device waits: 2 s
+
+// error bits written to the workspace error word
+enum : int { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_BAD_EXPERT = 4, ERR_BAD_SHAPE = 8 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ uint64_t globaltimer()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- mbarrier + bulk async copy (TMA engine, no tensor map) -----------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and the caller records an error and leaves its loop) once WAIT_TIMEOUT_NS passed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true)
+    {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer() - t0 > (uint64_t) WAIT_TIMEOUT_NS) return false;
+    }
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes and addresses 16-byte aligned)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---- trellis tile decode ---------------------------------------------------------------------------------------------
+
+// Per-lane constants for decoding lane `lane`'s 8 stream weights of a K-bit tile: the two 32-bit words holding its
+// (7K+16)-bit window, a right pre-shift that brings every state's shift below 32, and the 8 state shifts.
+template <int K>
+struct LaneDecode
+{
+    uint32_t off_hi, off_lo, pre;
+    uint32_t sh[8];
+    __device__ __forceinline__ void init(int lane)
+    {
+        constexpr int bits = 256 * K, words = 8 * K;
+        const int start = (8 * lane * K + K - 16 + bits) % bits;     // first bit of weight 8*lane's window
+        const int wa = start / 32, rs = start % 32;
+        off_hi = 4u * wa;
+        off_lo = 4u * ((wa + 1) % words);
+        const int shift0 = 48 - rs;                                   // shift of state 0 in (hi:lo)
+        pre = shift0 > 31 ? shift0 - 31 : 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sh[j] = uint32_t(shift0 - (int) pre - K * j);
+    }
+};
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// fp16 pair (lo = a, hi = b) of codebook weights from two byte sums, one fp16 rounding (hfma), ft_core.h:81-83
+__device__ __forceinline__ uint32_t codebook_pair(uint32_t sa, uint32_t sb)
+{
+    const uint32_t hb = __byte_perm(sa, sb, 0x5410);                // half(1024+sa) | half(1024+sb) << 16
+    __half2 h = *reinterpret_cast<const __half2*>(&hb);
+    const __half2 kinv = __halves2half2(__ushort_as_half(KINV_BITS), __ushort_as_half(KINV_BITS));
+    const __half2 kbias = __halves2half2(__ushort_as_half(KBIAS_BITS), __ushort_as_half(KBIAS_BITS));
+    h = __hfma2(h, kinv, kbias);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Decode lane's 8 weights of the tile at `tile` (shared memory) into the mma.m16n8k16 A fragment of W^T:
+// a[0] = (j0, j1), a[1] = (j4, j5), a[2] = (j2, j3), a[3] = (j6, j7).
+template <int K>
+__device__ __forceinline__ void decode_frag(const uint8_t* tile, const LaneDecode<K>& L, uint32_t a[4])
+{
+    const uint32_t hi = lds32(tile + L.off_hi), lo = lds32(tile + L.off_lo);
+    const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
+    const uint32_t hi2 = hi >> L.pre;
+    uint32_t s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+    {
+        const uint32_t st = __funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu;
+        s[j] = __dp4a(st * MUL1, 0x01010101u, 0x6400u);              // 0x6400 + bytesum = fp16 bits of 1024 + s
+    }
+    a[0] = codebook_pair(s[0], s[1]);
+    a[1] = codebook_pair(s[4], s[5]);
+    a[2] = codebook_pair(s[2], s[3]);
+    a[3] = codebook_pair(s[6], s[7]);
+}
+
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- 128-point transforms on one warp (lane holds v[q] = element lane + 32 q) ------------------------------------------
+
+// Unnormalised Walsh-Hadamard butterfly in the reference's stage order w = 1, 2, ..., 64 (ft_core.h:89-94):
+// v[i] = a + c, v[i + w] = a - c with a = v[i], c = v[i + w]. Same fp32 operations, same order.
+__device__ __forceinline__ void had128_warp(float v[4], int lane)
+{
+#pragma unroll
+    for (int w = 1; w < 32; w <<= 1)
+    {
+        const bool upper = (lane & w) != 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+        {
+            const float o = __shfl_xor_sync(0xffffffffu, v[q], w);
+            v[q] = upper ? (o - v[q]) : (v[q] + o);
+        }
+    }
+    {   // w = 32: pairs (q0, q1), (q2, q3)
+        const float a0 = v[0], c0 = v[1], a1 = v[2], c1 = v[3];
+        v[0] = a0 + c0; v[1] = a0 - c0; v[2] = a1 + c1; v[3] = a1 - c1;
+    }
+    {   // w = 64: pairs (q0, q2), (q1, q3)
+        const float a0 = v[0], c0 = v[2], a1 = v[1], c1 = v[3];
+        v[0] = a0 + c0; v[2] = a0 - c0; v[1] = a1 + c1; v[3] = a1 - c1;
+    }
+}
+
+__device__ __forceinline__ float r16(float f) { return __half2float(__float2half_rn(f)); }
+
+// silu(g) * u with the reference's optional clamp (ft_core.h:122-132). exp is evaluated in double and rounded, so the
+// fp32 value matches a correctly rounded expf.
+__device__ __forceinline__ float act_mul(float g, float u, float limit)
+{
+    const float e = (float) exp(-(double) g);
+    float x = g / (1.0f + e);
+    if (limit != 0.0f) { u = fminf(fmaxf(u, -limit), limit); x = fminf(x, limit); }
+    return x * u;
+}
+
+}  // namespace glmx

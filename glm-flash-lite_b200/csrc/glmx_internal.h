@@ -1,0 +1,61 @@
+// Internal (non-ABI) declarations shared by the .cu files of libglmx.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/glmx.h"
+
+namespace glmx {
+
+// Registered layer: device pointer tables of an HBM-resident expert bank (one entry per expert; the shared expert,
+// when present, is the last entry).
+struct Layer
+{
+    int H = 0, I = 0, E = 0, E_total = 0, has_shared = 0;
+    int bits[3] = { 3, 3, 3 };
+    float act_limit = 0.0f;
+    int device = 0;
+    uint64_t* d_trellis = nullptr;     // device [E_total][3] addresses (gate, up, down)
+    const uint16_t* suh[3] = {};       // device fp16 [E_total][k]
+    const uint16_t* svh[3] = {};       // device fp16 [E_total][n]
+};
+
+// Per-call routing plan, written by the route kernel and read by the later kernels.
+struct Plan
+{
+    int P;       // valid routed picks (rows 0..P-1, expert-major)
+    int R;       // rows including the shared expert's rows
+    int J;       // jobs (<= MAXM rows of one expert)
+    int S_gu;    // split-K of the gate/up kernel
+    int S_d;     // split-K of the down kernel
+    int ntok, topk, pad;
+};
+
+// Workspace layout of one forward call (byte offsets from the workspace base, 256-byte aligned).
+struct WsLayout
+{
+    size_t plan, err, offsets, row_token, row_expert, row_pick, row_weight, pick_row, jobs;
+    size_t cnt_gu, cnt_d, xg, xu, xd, yrow, partials;
+    size_t total;
+    int rows_max, jobs_max, part_slots;
+};
+
+WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas);
+
+// grid size of the persistent GEMV kernels on the current device
+int gemv_grid_ctas(const Layer& L);
+
+void set_error(const std::string& msg);
+
+// launchers (return cudaError_t of the launch)
+cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
+                         uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);
+cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,
+                                  int out_dtype, int accumulate, uint8_t* ws, const WsLayout& lay, int grid_ctas,
+                                  cudaStream_t st, void* const* events);
+cudaError_t launch_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, cudaStream_t st);
+
+}  // namespace glmx

@@ -1,0 +1,228 @@
+// Top-k token split: expert-major grouping of the router's picks (one CTA).
+//
+// Reference behaviour: moe_forward builds jobs by walking tokens in order and, per token, its picks in order,
+// appending (token, weight) to the expert's current job and opening a new job once it holds MAXM = 8 tokens
+// (kernels/cpu_avx2/ft_core.h:1344-1349). tier_forward skips picks with sel < 0 (ft_tier_ext.cpp:896-898).
+// Here the rows are laid out expert-major (expert ascending, pick index ascending = token order), which is the
+// canonical order of the reference's grouped rows, and jobs are consecutive runs of <= 8 rows of one expert, so
+// each job holds exactly the tokens of the corresponding reference job.
+//
+// The stable scatter processes the picks in chunks of 1024: __match_any_sync gives each pick its rank among equal
+// experts in its warp, a per-(warp, expert) count table gives the rank across warps, a running base per expert
+// carries ranks across chunks. This is the warp-ballot prefix of ft_split_fast (kernels/k110/ft_split_fast.cu:153-175)
+// generalised from one warp to the whole block.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "glmx_common.cuh"
+#include "glmx_internal.h"
+
+namespace glmx {
+
+namespace {
+
+constexpr int RT = 1024;   // threads of the route CTA
+
+struct RouteArgs
+{
+    const void* sel; int sel_i64;
+    const void* w; int w_dtype;
+    int ntok, topk, E, has_shared;
+    int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
+    int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
+    int grid_ctas, part_slots;
+    Plan* plan;
+    int* offsets; int* row_token; int* row_expert; int* row_pick; float* row_weight; int* pick_row; int4* jobs;
+    int* cnt_gu; int* cnt_d; int* err;
+};
+
+__device__ __forceinline__ int load_sel(const RouteArgs& a, int p)
+{
+    return a.sel_i64 ? (int) max((long long) -1, min((long long) 0x7fffffff, reinterpret_cast<const long long*>(a.sel)[p]))
+                     : reinterpret_cast<const int*>(a.sel)[p];
+}
+
+__device__ __forceinline__ float load_w(const RouteArgs& a, int p)
+{
+    if (a.w_dtype == GLMX_F16) return __half2float(reinterpret_cast<const __half*>(a.w)[p]);
+    if (a.w_dtype == GLMX_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.w)[p]);
+    return reinterpret_cast<const float*>(a.w)[p];
+}
+
+// exclusive scan of one int per thread (RT threads); returns the exclusive prefix, *total = sum
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total)
+{
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+    {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[wid] = x;
+    __syncthreads();
+    if (wid == 0)
+    {
+        int s = warp_sums[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+        {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        warp_sums[lane] = s;   // inclusive over warps
+    }
+    __syncthreads();
+    const int before = (wid ? warp_sums[wid - 1] : 0) + x - v;
+    *total = warp_sums[31];
+    __syncthreads();
+    return before;
+}
+
+// Split-K factor: the smallest divisor d of `stages` (each part >= 2 stages) with units * d >= target, never more
+// items than `slots` partial-sum slots.
+__device__ int pick_split(long long units, int stages, int target, int slots)
+{
+    int s = 1;
+    if (units >= target) return 1;
+    for (int d = 2; d <= stages / 2; ++d)
+    {
+        if (stages % d) continue;
+        if (units * d > slots) break;
+        s = d;
+        if (units * d >= target) break;
+    }
+    return s;
+}
+
+__global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
+{
+    extern __shared__ int sm[];
+    const int E = a.E;
+    int* cnt = sm;                                   // [E]
+    int* base = cnt + E;                             // [E]
+    unsigned short* wcnt = reinterpret_cast<unsigned short*>(base + E);   // [32][E]
+    __shared__ int warp_sums[32];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int n = a.ntok * a.topk;
+
+    for (int e = tid; e < E; e += RT) cnt[e] = 0;
+    for (int i = tid; i < 32 * E; i += RT) wcnt[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < n; p += RT)
+    {
+        const int e = load_sel(a, p);
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+
+    // offsets and jobs (E <= RT: one expert per thread)
+    const int c = tid < E ? cnt[tid] : 0;
+    int P;
+    const int off = block_exclusive_scan(c, warp_sums, &P);
+    const int nj = (c + MAXM - 1) / MAXM;
+    int Jr;
+    const int joff = block_exclusive_scan(nj, warp_sums, &Jr);
+    if (tid < E)
+    {
+        a.offsets[tid] = off;
+        base[tid] = off;
+        for (int q = 0; q < nj; ++q) a.jobs[joff + q] = make_int4(tid, off + q * MAXM, min(MAXM, c - q * MAXM), 0);
+    }
+    if (tid == 0) a.offsets[E] = P;
+    const int nsh = a.has_shared ? a.ntok : 0;
+    const int Jsh = (nsh + MAXM - 1) / MAXM;
+    for (int q = tid; q < Jsh; q += RT) a.jobs[Jr + q] = make_int4(E, P + q * MAXM, min(MAXM, nsh - q * MAXM), 0);
+    for (int t = tid; t < nsh; t += RT)
+    {
+        a.row_token[P + t] = t; a.row_expert[P + t] = E; a.row_pick[P + t] = -1; a.row_weight[P + t] = 1.0f;
+    }
+    __syncthreads();
+
+    // stable scatter, chunks of RT picks
+    const unsigned lt = (1u << lane) - 1u;
+    for (int c0 = 0; c0 < n; c0 += RT)
+    {
+        const int p = c0 + tid;
+        int e = -1;
+        float wt = 0.0f;
+        if (p < n)
+        {
+            e = load_sel(a, p);
+            wt = load_w(a, p);
+            if (e < 0 || e >= E) { a.pick_row[p] = -1; e = -1; }
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int lrank = __popc(peers & lt);
+        if (e >= 0 && lrank == 0) wcnt[wid * E + e] = (unsigned short) __popc(peers);
+        __syncthreads();
+        if (e >= 0)
+        {
+            int pre = 0;
+            for (int w2 = 0; w2 < wid; ++w2) pre += wcnt[w2 * E + e];
+            const int r = base[e] + pre + lrank;
+            a.row_token[r] = p / a.topk; a.row_expert[r] = e; a.row_pick[r] = p; a.row_weight[r] = wt;
+            a.pick_row[p] = r;
+        }
+        __syncthreads();
+        for (int e2 = tid; e2 < E; e2 += RT)
+        {
+            int s = 0;
+            for (int w2 = 0; w2 < 32; ++w2) { s += wcnt[w2 * E + e2]; wcnt[w2 * E + e2] = 0; }
+            base[e2] += s;
+        }
+        __syncthreads();
+    }
+
+    const int J = Jr + Jsh;
+    for (int i = tid; i < J * a.nb_gu; i += RT) a.cnt_gu[i] = 0;
+    for (int i = tid; i < J * a.nb_d; i += RT) a.cnt_d[i] = 0;
+    if (tid == 0)
+    {
+        Plan pl;
+        pl.P = P; pl.R = P + nsh; pl.J = J;
+        pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_slots);
+        pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_slots);
+        pl.ntok = a.ntok; pl.topk = a.topk; pl.pad = 0;
+        *a.plan = pl;
+        *a.err = 0;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
+                         uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st)
+{
+    RouteArgs a;
+    a.sel = sel; a.sel_i64 = sel_i64; a.w = w; a.w_dtype = w_dtype;
+    a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared;
+    a.nb_gu = L.I / 128; a.nb_d = L.H / 128; a.kq_gu = L.H / 128; a.kq_d = L.I / 128;
+    a.grid_ctas = grid_ctas;
+    a.part_slots = lay.part_slots;
+    a.plan = reinterpret_cast<Plan*>(ws + lay.plan);
+    a.offsets = reinterpret_cast<int*>(ws + lay.offsets);
+    a.row_token = reinterpret_cast<int*>(ws + lay.row_token);
+    a.row_expert = reinterpret_cast<int*>(ws + lay.row_expert);
+    a.row_pick = reinterpret_cast<int*>(ws + lay.row_pick);
+    a.row_weight = reinterpret_cast<float*>(ws + lay.row_weight);
+    a.pick_row = reinterpret_cast<int*>(ws + lay.pick_row);
+    a.jobs = reinterpret_cast<int4*>(ws + lay.jobs);
+    a.cnt_gu = reinterpret_cast<int*>(ws + lay.cnt_gu);
+    a.cnt_d = reinterpret_cast<int*>(ws + lay.cnt_d);
+    a.err = reinterpret_cast<int*>(ws + lay.err);
+    const size_t smem = sizeof(int) * 2 * L.E + sizeof(unsigned short) * 32 * L.E + 16;
+    static bool attr_set[64] = {};
+    if (L.device < 0 || L.device >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[L.device])
+    {
+        cudaError_t e = cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[L.device] = true;
+    }
+    route_kernel<<<1, RT, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace glmx

@@ -1,0 +1,6 @@
+"""glmx: B200-native routed-expert MoE layer over EXL3 trellis-coded experts (drop-in for glm-flash-lite's expert
+tier). The compute lives in libglmx.so (include/glmx.h); this package is the PyTorch-side host."""
+from ._lib import GlmxError, load  # noqa: F401
+from .layer import MoELayer, decode_tiles  # noqa: F401
+
+__all__ = ["MoELayer", "decode_tiles", "GlmxError", "load"]

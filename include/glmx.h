@@ -1,0 +1,116 @@
+/* glmx - B200 (sm_100a) routed-expert MoE layer over EXL3 trellis-coded experts.
+ *
+ * C ABI of libglmx.so. Plain pointers and sizes; every device pointer is a CUDA device address on the current
+ * device, `stream` is a cudaStream_t (NULL = the legacy default stream). Every entry point returns 0 on success and
+ * a negative GLMX_E_* code on failure; glmx_last_error() then describes the failure (thread-local).
+ * Nothing here allocates device memory except glmx_layer_create (the layer's pointer tables). Scratch memory of a
+ * forward call is the caller's workspace (glmx_workspace_bytes).
+ *
+ * Each entry point names the reference interface it replaces (nkeilar/glm-flash-lite, file:line).
+ */
+#ifndef GLMX_H
+#define GLMX_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLMX_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GLMX_API __attribute__((visibility("default")))
+#else
+#define GLMX_API
+#endif
+
+#define GLMX_OK 0
+#define GLMX_E_ARG -1       /* invalid argument or shape */
+#define GLMX_E_CUDA -2      /* CUDA runtime error (launch or memory) */
+#define GLMX_E_DEVICE -3    /* a device-side check failed (bounded wait expired, bad expert id): see glmx_check */
+#define GLMX_E_WORKSPACE -4 /* workspace too small */
+
+/* dtypes */
+#define GLMX_F16 0
+#define GLMX_F32 1
+#define GLMX_BF16 2
+#define GLMX_I32 3
+#define GLMX_I64 4
+
+/* numeric modes, same numbering as the reference's moe_forward (kernels/cpu_avx2/ft_core.h:822-823) */
+#define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights (GPU-exact), fp32 tensor-core accumulation */
+
+typedef struct glmx_layer glmx_layer;
+
+/* One MoE layer's routed experts (+ optional shared expert as the last entry), HBM-resident, native EXL3 layout:
+ * tile (tk, tn) of a [k x n] projection at byte (tk * (n/16) + tn) * 32 * bits. Replaces the registration of
+ * tier_add_layer(li, ptrs int64 [E,3], suh_g, svh_g, suh_u, svh_u, suh_d, svh_d) (kernels/cpu_avx2/ft_tier_ext.cpp:159-183)
+ * and the per-expert pointer tables exllamav3 keeps (ptrs_trellis, glm53/expert_cache.py:603-616). */
+typedef struct
+{
+    int hidden;                       /* H, multiple of 128 */
+    int intermediate;                 /* I, multiple of 128 */
+    int n_experts;                    /* routed experts E (<= 1024) */
+    int has_shared;                   /* 1: a shared expert is stored as entry E */
+    int bits[3];                      /* trellis bits per weight of gate, up, down: 2, 3 or 4 */
+    const uint64_t* trellis;          /* HOST array [(E + has_shared) * 3] of device addresses (gate, up, down), 16-byte aligned */
+    const void* suh[3];               /* device fp16 [(E + has_shared), k] input sign/scale vectors per projection */
+    const void* svh[3];               /* device fp16 [(E + has_shared), n] output scale vectors per projection */
+    float act_limit;                  /* SwiGLU clamp (0 = off), tier_set_act_limit (ft_tier_ext.cpp:635) */
+} glmx_layer_desc;
+
+GLMX_API int glmx_version(void);
+GLMX_API const char* glmx_last_error(void);
+
+GLMX_API int glmx_layer_create(const glmx_layer_desc* desc, glmx_layer** out);
+GLMX_API int glmx_layer_destroy(glmx_layer* layer);
+/* tier_set_act_limit (kernels/cpu_avx2/ft_tier_ext.cpp:635) */
+GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
+
+/* Bytes of caller-provided device workspace a forward over `ntok` tokens with `topk` picks each needs. */
+GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk);
+
+/* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
+ * (expert, token), pick -> row map, jobs of <= 8 rows). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
+ * kernels/k110/ft_split_fast.cu:200-235) and the job grouping of moe_forward (kernels/cpu_avx2/ft_core.h:1344-1349).
+ * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64); ids outside [0, E) are skipped.
+ * w: device [ntok, topk] fp32 / fp16 / bf16. */
+GLMX_API int glmx_route(const glmx_layer* layer, const void* sel, int sel_dtype, const void* w, int w_dtype, int ntok, int topk,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Locate one routing array inside a workspace filled by glmx_route (for tests and callers that reuse the split):
+ * which = 0 offsets int32 [E+1], 1 row_token int32 [R], 2 row_weight fp32 [R], 3 pick_row int32 [ntok*topk],
+ * 4 jobs int32x4 [J] (expert, row0, m, 0), 5 plan int32 [8] (P, R, J, S_gu, S_d, ntok, topk, 0), 6 row_pick int32 [R]. */
+GLMX_API int glmx_workspace_array(const glmx_layer* layer, int ntok, int topk, int which, size_t* offset_bytes);
+
+/* Whole routed-MoE layer on the GPU: split -> gate/up dequant-GEMV + SiLU*up -> down dequant-GEMV -> weighted
+ * combine (+ shared expert, weight 1). out [ntok, H] (fp32 or fp16) = sum over token picks of w * expert(x) + shared(x);
+ * accumulate = 1 adds into out instead (ft_combine's `out += partial`, kernels/cpu_avx2/ft_tier_cu.cu:226-233).
+ * Replaces tier_forward(li, x fp32 [m,H], sel int32 [m,k], w fp32 [m,k], mode) (kernels/cpu_avx2/ft_tier_ext.cpp:864-904)
+ * and the GPU expert path it stands beside (exllamav3 BlockSparseMLP experts). x: device [ntok, H] fp16 / fp32 / bf16. */
+GLMX_API int glmx_moe_forward(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                     const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* glmx_moe_forward that also records `events` (GLMX_PHASES cudaEvent_t, or NULL entries to skip) on `stream` before the
+ * split, after the split, after the input transform, after gate/up, after down and after the combine, so a caller
+ * can time each kernel on the launching stream. */
+#define GLMX_PHASES 6
+GLMX_API int glmx_moe_forward_timed(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
+                     int sel_dtype, const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
+                     void* workspace, size_t workspace_bytes, void* stream, void* const* events);
+
+/* Known-answer entry for the trellis decode: `ntiles` tiles of 32*bits bytes (device) -> fp16 bit patterns
+ * [ntiles, 16, 16] (row r = input index, column c = output index), as dense_weights (kernels/cpu_avx2/ft_core.h:1657-1672). */
+GLMX_API int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, void* stream);
+
+/* Synchronise `stream` and read the device error word of a workspace (bounded waits that expired, bad expert ids):
+ * returns GLMX_OK or GLMX_E_DEVICE; *flags receives the raw bits. The reference surfaces device failures through
+ * sticky ctrl words and stats (kernels/cpu_avx2/ft_tier_cu.cu:33-52, 176-193). */
+GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* workspace, void* stream, int* flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,241 @@
+/* Test infrastructure only: CPU restatement of the reference's routed-expert path (see ft_oracle.h).
+ * Plain C11, scalar, single-threaded. Reference: nkeilar/glm-flash-lite kernels/cpu_avx2/ft_core.h. */
+#include "ft_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ft_core.h:28-40 */
+#define MUL1 0x83DCD12Du
+static const float HAD = 0.088388347648f;
+
+static int PERM[256];
+static float CODEBOOK_EXACT[1021];   /* s -> fp16-rounded weight (as fp32) */
+static float CODEBOOK_AFFINE[1021];  /* s -> unrounded fma(1024+s, KINV, KBIAS), exact in fp32 */
+static uint16_t BYTESUM[65536];     /* st -> bytesum(st * MUL1), a cache of fto_bytesum */
+static float KINV, KBIAS;
+static int inited = 0;
+
+uint16_t fto_f2h(float f) { _Float16 h = (_Float16) f; uint16_t b; memcpy(&b, &h, 2); return b; }
+float fto_h2f(uint16_t b) { _Float16 h; memcpy(&h, &b, 2); return (float) h; }
+static float r16(float f) { return fto_h2f(fto_f2h(f)); }
+
+/* ft_core.h:48-61 init_perm */
+void fto_init(void)
+{
+    if (inited) return;
+    for (int t = 0; t < 32; ++t) {
+        const int r0 = (t % 4) * 2, r1 = r0 + 1, r2 = r0 + 8, r3 = r0 + 9;
+        const int c0 = t / 4, c1 = c0 + 8;
+        const int rc[8] = { r0 * 16 + c0, r1 * 16 + c0, r2 * 16 + c0, r3 * 16 + c0,
+                            r0 * 16 + c1, r1 * 16 + c1, r2 * 16 + c1, r3 * 16 + c1 };
+        for (int j = 0; j < 8; ++j) PERM[t * 8 + j] = rc[j];
+    }
+    KINV = fto_h2f(0x1eee);
+    KBIAS = fto_h2f(0xc931);
+    for (int s = 0; s <= 1020; ++s) {
+        CODEBOOK_AFFINE[s] = fmaf((float) (1024 + s), KINV, KBIAS);
+        CODEBOOK_EXACT[s] = r16(CODEBOOK_AFFINE[s]);
+    }
+    for (int st = 0; st < 65536; ++st) BYTESUM[st] = (uint16_t) fto_bytesum((uint16_t) st);
+    inited = 1;
+}
+
+int fto_perm(int i) { fto_init(); return PERM[i]; }
+
+/* little-endian 32-bit word i of the tile (ft_core.h:63 ld32) */
+static uint32_t ld32(const uint8_t* p, int i)
+{
+    return (uint32_t) p[4 * i] | ((uint32_t) p[4 * i + 1] << 8) | ((uint32_t) p[4 * i + 2] << 16) | ((uint32_t) p[4 * i + 3] << 24);
+}
+
+/* ft_core.h:65-73 state_scalar with BITS = K */
+uint16_t fto_state(const uint8_t* tile, int K, int t)
+{
+    const int words32 = K * 256 / 32;
+    const int b0 = t * K + K - 16 + 256 * K;
+    const int b1 = b0 + 16;
+    const int shift = ((b1 - 1) / 32 + 1) * 32 - b1;
+    const uint64_t merged = ((uint64_t) ld32(tile, (b0 / 32) % words32) << 32) | ld32(tile, ((b1 - 1) / 32) % words32);
+    return (uint16_t) (merged >> shift);
+}
+
+/* ft_core.h:75-79 */
+int fto_bytesum(uint16_t st)
+{
+    const uint32_t x = (uint32_t) st * MUL1;
+    return (int) ((x & 0xff) + ((x >> 8) & 0xff) + ((x >> 16) & 0xff) + (x >> 24));
+}
+
+/* ft_core.h:81-83 w_gpu_s */
+uint16_t fto_codebook_h(int s) { fto_init(); return fto_f2h(CODEBOOK_EXACT[s]); }
+
+void fto_decode_tile(const uint8_t* tile, int K, uint16_t* w16)
+{
+    fto_init();
+    for (int i = 0; i < 256; ++i) w16[PERM[i]] = fto_f2h(CODEBOOK_EXACT[fto_bytesum(fto_state(tile, K, i))]);
+}
+
+/* ft_core.h:1657-1672 dense_weights (mode 1) and the unrounded codebook (mode 0) */
+static void dense_mode(const uint8_t* tr, int K, int k, int n, int mode, float* W)
+{
+    fto_init();
+    const float* cb = mode == 0 ? CODEBOOK_AFFINE : CODEBOOK_EXACT;
+    const int tn = n / 16, tb = 32 * K;
+    for (int tk = 0; tk < k / 16; ++tk)
+        for (int t = 0; t < tn; ++t) {
+            const uint8_t* tile = tr + ((size_t) tk * tn + t) * tb;
+            for (int i = 0; i < 256; ++i) {
+                const int rc = PERM[i];
+                W[(size_t) (tk * 16 + rc / 16) * n + t * 16 + rc % 16] = cb[BYTESUM[fto_state(tile, K, i)]];
+            }
+        }
+}
+
+void fto_dense(const uint8_t* tr, int K, int k, int n, float* W) { dense_mode(tr, K, k, n, 1, W); }
+
+/* ft_core.h:89-94 */
+void fto_had128(float* v)
+{
+    for (int w = 1; w < 128; w *= 2)
+        for (int b = 0; b < 128; b += 2 * w)
+            for (int i = 0; i < w; ++i) { const float a = v[b + i], c = v[b + w + i]; v[b + i] = a + c; v[b + w + i] = a - c; }
+}
+
+/* ft_core.h:96-102 */
+void fto_prep_block(const float* x, const uint16_t* suh, float* xt)
+{
+    for (int i = 0; i < 128; ++i) xt[i] = x[i] * fto_h2f(suh[i]);
+    fto_had128(xt);
+    for (int i = 0; i < 128; ++i) xt[i] = r16(xt[i] * HAD);
+}
+
+/* ft_core.h:104-110 */
+void fto_out_block(float* y, const uint16_t* svh)
+{
+    for (int i = 0; i < 128; ++i) y[i] = r16(y[i]);
+    fto_had128(y);
+    for (int i = 0; i < 128; ++i) { const float t = y[i] * HAD; y[i] = r16(t * fto_h2f(svh[i])); }
+}
+
+/* ft_core.h:122-132 */
+float fto_act_mul(float g, float u, float limit)
+{
+    float x = g / (1.0f + expf(-g));
+    if (limit != 0.0f) { u = fminf(fmaxf(u, -limit), limit); x = fminf(x, limit); }
+    return x * u;
+}
+
+/* ft_core.h:1674-1682 ref_linear, m tokens at once (fp64 accumulation) */
+void fto_linear(const uint8_t* tr, int K, const uint16_t* suh, const uint16_t* svh, int k, int n,
+                const float* W, int mode, const float* x, int m, float* y)
+{
+    float* Wl = NULL;
+    if (!W) { Wl = (float*) malloc(sizeof(float) * (size_t) k * n); dense_mode(tr, K, k, n, mode, Wl); W = Wl; }
+    float* xt = (float*) malloc(sizeof(float) * (size_t) k);
+    double* acc = (double*) malloc(sizeof(double) * (size_t) n);
+    for (int t = 0; t < m; ++t) {
+        const float* xr = x + (size_t) t * k;
+        float* yr = y + (size_t) t * n;
+        for (int b = 0; b < k / 128; ++b) fto_prep_block(xr + b * 128, suh + b * 128, xt + b * 128);
+        for (int j = 0; j < n; ++j) acc[j] = 0.0;
+        for (int kk = 0; kk < k; ++kk) {
+            const double xv = xt[kk];
+            const float* wr = W + (size_t) kk * n;
+            for (int j = 0; j < n; ++j) acc[j] += xv * wr[j];
+        }
+        for (int j = 0; j < n; ++j) yr[j] = (float) acc[j];
+        for (int b = 0; b < n / 128; ++b) fto_out_block(yr + b * 128, svh + b * 128);
+    }
+    free(acc); free(xt); free(Wl);
+}
+
+/* ft_core.h:1684-1691 ref_expert (generic I; activation rounding point of ft_core.h:980) */
+void fto_expert(const fto_expert_t* ex, int H, int I, int mode, float act_limit, const float* x, int m, float* y)
+{
+    float* g = (float*) malloc(sizeof(float) * (size_t) m * I);
+    float* u = (float*) malloc(sizeof(float) * (size_t) m * I);
+    fto_linear(ex->tr[0], ex->K[0], ex->suh[0], ex->svh[0], H, I, NULL, mode, x, m, g);
+    fto_linear(ex->tr[1], ex->K[1], ex->suh[1], ex->svh[1], H, I, NULL, mode, x, m, u);
+    for (size_t i = 0; i < (size_t) m * I; ++i) g[i] = r16(fto_act_mul(g[i], u[i], act_limit));
+    fto_linear(ex->tr[2], ex->K[2], ex->suh[2], ex->svh[2], I, H, NULL, mode, g, m, y);
+    free(g); free(u);
+}
+
+/* Expert-major grouping: rows sorted by (expert asc, pick index asc). Within an expert the pick index order
+ * is token order, which is the order ft_core.h:1344-1349 appends tokens to an expert's jobs. */
+int fto_group(const int32_t* sel, const float* w, int ntok, int topk, int E,
+              int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* row_pick, int32_t* pick_row)
+{
+    const int n = ntok * topk;
+    for (int e = 0; e <= E; ++e) offsets[e] = 0;
+    for (int p = 0; p < n; ++p) if (sel[p] >= 0 && sel[p] < E) offsets[sel[p] + 1]++;
+    for (int e = 0; e < E; ++e) offsets[e + 1] += offsets[e];
+    int32_t* fill = (int32_t*) calloc((size_t) (E > 0 ? E : 0) + 1, sizeof(int32_t));
+    for (int p = 0; p < n; ++p) {
+        const int e = sel[p];
+        if (e < 0 || e >= E) { pick_row[p] = -1; continue; }
+        const int r = offsets[e] + fill[e]++;
+        row_token[r] = p / topk; row_weight[r] = w[p]; row_pick[r] = p; pick_row[p] = r;
+    }
+    free(fill);
+    return offsets[E];
+}
+
+/* ft_core.h:1344-1349 */
+int fto_jobs_ref(const int32_t* sel, const float* w, int ntok, int topk, int E, int maxm,
+                 int32_t* job_e, int32_t* job_m, int32_t* job_tok, float* job_w)
+{
+    int32_t* jid = (int32_t*) malloc(sizeof(int32_t) * ((size_t) (E > 0 ? E : 0) + 1));
+    for (int e = 0; e < E; ++e) jid[e] = -1;
+    int nj = 0;
+    for (int t = 0; t < ntok; ++t)
+        for (int kk = 0; kk < topk; ++kk) {
+            const int e = sel[t * topk + kk];
+            if (e < 0 || e >= E) continue;
+            if (jid[e] < 0 || job_m[jid[e]] == maxm) { jid[e] = nj; job_e[nj] = e; job_m[nj] = 0; ++nj; }
+            const int j = jid[e];
+            job_tok[j * maxm + job_m[j]] = t; job_w[j * maxm + job_m[j]] = w[t * topk + kk]; job_m[j]++;
+        }
+    free(jid);
+    return nj;
+}
+
+void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* shared, int H, int I, int mode,
+                     float act_limit, const float* x, int ntok, const int32_t* sel, const float* w, int topk, float* out)
+{
+    const int n = ntok * topk;
+    int32_t* offsets = (int32_t*) malloc(sizeof(int32_t) * ((size_t) (E > 0 ? E : 0) + 1));
+    int32_t* row_token = (int32_t*) malloc(sizeof(int32_t) * (size_t) (n > 0 ? n : 1));
+    float* row_weight = (float*) malloc(sizeof(float) * (size_t) (n > 0 ? n : 1));
+    int32_t* row_pick = (int32_t*) malloc(sizeof(int32_t) * (size_t) (n > 0 ? n : 1));
+    int32_t* pick_row = (int32_t*) malloc(sizeof(int32_t) * (size_t) (n > 0 ? n : 1));
+    const int P = fto_group(sel, w, ntok, topk, E, offsets, row_token, row_weight, row_pick, pick_row);
+    float* yrow = (float*) malloc(sizeof(float) * (size_t) (P > 0 ? P : 1) * H);
+    float* xs = (float*) malloc(sizeof(float) * (size_t) (P > 0 ? P : 1) * H);   /* one expert can take every pick */
+    for (int e = 0; e < E; ++e) {
+        const int r0 = offsets[e], m = offsets[e + 1] - r0;
+        if (!m) continue;
+        for (int i = 0; i < m; ++i) memcpy(xs + (size_t) i * H, x + (size_t) row_token[r0 + i] * H, sizeof(float) * H);
+        fto_expert(&experts[e], H, I, mode, act_limit, xs, m, yrow + (size_t) r0 * H);
+    }
+    float* ysh = NULL;
+    if (shared && ntok) {
+        ysh = (float*) malloc(sizeof(float) * (size_t) ntok * H);
+        fto_expert(shared, H, I, mode, act_limit, x, ntok, ysh);
+    }
+    for (int t = 0; t < ntok; ++t) {
+        float* o = out + (size_t) t * H;
+        for (int c = 0; c < H; ++c) o[c] = 0.0f;
+        for (int kk = 0; kk < topk; ++kk) {
+            const int r = pick_row[t * topk + kk];
+            if (r < 0) continue;
+            const float wt = row_weight[r];
+            const float* y = yrow + (size_t) r * H;
+            for (int c = 0; c < H; ++c) o[c] += wt * y[c];
+        }
+        if (ysh) { const float* y = ysh + (size_t) t * H; for (int c = 0; c < H; ++c) o[c] += y[c]; }
+    }
+    free(ysh); free(xs); free(yrow); free(pick_row); free(row_pick); free(row_weight); free(row_token); free(offsets);
+}

@@ -1,0 +1,82 @@
+/* Test infrastructure only: CPU restatement of the reference's routed-expert path.
+ *
+ * This is the checker for the CUDA product in glm-flash-lite_b200/. Only tests/, the smoke check in
+ * __graft_entry__.py and the cpu_baseline leg of bench.py may load it. Nothing in the product links it.
+ *
+ * Every function restates code from nkeilar/glm-flash-lite kernels/cpu_avx2/ft_core.h (cited per function).
+ * The trellis bit width K is a parameter here; the reference fixes K=3 (ft_core.h:30-31). K=2/4 follow the
+ * same formula with K substituted and are not pinned by anything in the reference tree.
+ */
+#ifndef FT_ORACLE_H
+#define FT_ORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* PERM table, ft_core.h:48-61 (stream index -> r*16 + c inside the 16x16 tile) */
+void fto_init(void);
+int fto_perm(int i);
+
+/* ft_core.h:65-73 with BITS -> K: 16-bit trellis state of stream weight t of one tile (32*K bytes) */
+uint16_t fto_state(const uint8_t* tile, int K, int t);
+/* ft_core.h:75-79 */
+int fto_bytesum(uint16_t st);
+/* ft_core.h:81-83: fp16 bits of fp16(fma(1024 + s, KINV, KBIAS)) */
+uint16_t fto_codebook_h(int s);
+
+/* one tile -> 256 fp16 bit patterns in (r, c) row-major order, r = input row, c = output column */
+void fto_decode_tile(const uint8_t* tile, int K, uint16_t* w16);
+/* ft_core.h:1657-1672 dense_weights: [k][n] fp32 (fp16-valued) from a native-layout trellis tensor */
+void fto_dense(const uint8_t* tr, int K, int k, int n, float* W);
+
+/* fp16 helpers (IEEE binary16, round to nearest even) */
+uint16_t fto_f2h(float f);
+float fto_h2f(uint16_t h);
+
+/* ft_core.h:89-110 transforms on one 128-block */
+void fto_had128(float* v);
+void fto_prep_block(const float* x, const uint16_t* suh, float* xt);
+void fto_out_block(float* y, const uint16_t* svh);
+/* ft_core.h:122-132 act_mul; limit 0 = off */
+float fto_act_mul(float g, float u, float limit);
+
+/* One EXL3 linear in the reference's "GPU-exact weights, fp64 accumulation" form (ft_core.h:1674-1682).
+ * mode 1 = EXACT (fp16-rounded codebook weights), mode 0 = AFFINE (unrounded codebook KINV*(1024+s)+KBIAS).
+ * x: [m][k] fp16-valued fp32, y: [m][n]. W may be NULL (decoded on the fly) or a dense [k][n] array that
+ * matches the mode. */
+void fto_linear(const uint8_t* tr, int K, const uint16_t* suh, const uint16_t* svh, int k, int n,
+                const float* W, int mode, const float* x, int m, float* y);
+
+/* ft_core.h:1684-1691 ref_expert for m tokens: y[m][H] from x[m][H] (fp16-valued fp32) */
+typedef struct {
+    const uint8_t* tr[3];        /* gate, up, down trellis, native layout */
+    const uint16_t* suh[3];      /* fp16 [k] per projection */
+    const uint16_t* svh[3];      /* fp16 [n] per projection */
+    int K[3];                    /* bits per weight per projection */
+} fto_expert_t;
+void fto_expert(const fto_expert_t* ex, int H, int I, int mode, float act_limit, const float* x, int m, float* y);
+
+/* Expert-major grouping of the routed picks (ft_core.h:1344-1349 job rule, canonical expert-ascending form).
+ * sel/w: [ntok][topk]; picks with sel < 0 or sel >= E are skipped.
+ * outputs: offsets[E+1], row_token[P], row_weight[P], row_pick[P] (pick index t*topk+kk), pick_row[ntok*topk]
+ * (-1 for skipped picks). Returns P (number of valid picks). */
+int fto_group(const int32_t* sel, const float* w, int ntok, int topk, int E,
+              int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* row_pick, int32_t* pick_row);
+
+/* The reference's own job list (ft_core.h:1344-1349): first-touch expert order, <= maxm tokens per job.
+ * job_e/job_m: [njobs], job_tok/job_w: [njobs][maxm]. Returns njobs. */
+int fto_jobs_ref(const int32_t* sel, const float* w, int ntok, int topk, int E, int maxm,
+                 int32_t* job_e, int32_t* job_m, int32_t* job_tok, float* job_w);
+
+/* Whole layer: out[t] = sum over token t's picks in pick order of w * expert(x[t]) (fp32, ft_core.h:1020-1033
+ * with the sum taken in pick order), plus the shared expert (weight 1) when shared != NULL. */
+void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* shared, int H, int I, int mode,
+                     float act_limit, const float* x, int ntok, const int32_t* sel, const float* w, int topk, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,268 @@
+"""Test infrastructure only: ctypes access to the CPU restatement (oracle/_build/libftoracle.so, from ft_oracle.c)
+and to the shim over the reference's own ft_core.h (oracle/_ref/libftref.so).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference legs may import this module.
+Both libraries are built by oracle/Makefile (the reference shim only where the reference tree is present).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libftoracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libftref.so")
+
+_P = C.c_void_p
+_I = C.c_int
+_F = C.c_float
+
+
+def build(ref: bool = True) -> None:
+    """Build the restatement, and the reference shim when the reference tree exists."""
+    targets = ["oracle"]
+    if ref and os.path.isdir(os.environ.get("REF_KDIR", "/root/reference/kernels/cpu_avx2")):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(_P)
+
+
+class _Expert(C.Structure):
+    """fto_expert_t of ft_oracle.h"""
+    _fields_ = [("tr", _P * 3), ("suh", _P * 3), ("svh", _P * 3), ("K", _I * 3)]
+
+
+class Oracle:
+    """The restatement (ft_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build(ref=False)
+        L = C.CDLL(path)
+        L.fto_state.restype = C.c_uint16
+        L.fto_state.argtypes = [_P, _I, _I]
+        L.fto_bytesum.restype = _I
+        L.fto_bytesum.argtypes = [C.c_uint16]
+        L.fto_codebook_h.restype = C.c_uint16
+        L.fto_decode_tile.argtypes = [_P, _I, _P]
+        L.fto_dense.argtypes = [_P, _I, _I, _I, _P]
+        L.fto_had128.argtypes = [_P]
+        L.fto_prep_block.argtypes = [_P, _P, _P]
+        L.fto_out_block.argtypes = [_P, _P]
+        L.fto_act_mul.restype = _F
+        L.fto_act_mul.argtypes = [_F, _F, _F]
+        L.fto_linear.argtypes = [_P, _I, _P, _P, _I, _I, _P, _I, _P, _I, _P]
+        L.fto_expert.argtypes = [_P, _I, _I, _I, _F, _P, _I, _P]
+        L.fto_group.restype = _I
+        L.fto_group.argtypes = [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P]
+        L.fto_jobs_ref.restype = _I
+        L.fto_jobs_ref.argtypes = [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]
+        L.fto_moe_forward.argtypes = [_P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P, _I, _P]
+        L.fto_init()
+        self.L = L
+
+    # --- tiles -----------------------------------------------------------------------------------------------
+    def decode_tiles(self, tiles: np.ndarray, K: int) -> np.ndarray:
+        """tiles uint8 [n, 32K] -> fp16 bit patterns uint16 [n, 16, 16] (r, c)."""
+        tiles = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(-1, 32 * K)
+        out = np.empty((tiles.shape[0], 16, 16), dtype=np.uint16)
+        for i in range(tiles.shape[0]):
+            self.L.fto_decode_tile(_ptr(tiles[i]), K, _ptr(out[i]))
+        return out
+
+    def dense(self, tr: np.ndarray, K: int, k: int, n: int) -> np.ndarray:
+        W = np.empty((k, n), dtype=np.float32)
+        self.L.fto_dense(_ptr(np.ascontiguousarray(tr)), K, k, n, _ptr(W))
+        return W
+
+    def state(self, tile: np.ndarray, K: int, t: int) -> int:
+        return int(self.L.fto_state(_ptr(np.ascontiguousarray(tile)), K, t))
+
+    # --- transforms ------------------------------------------------------------------------------------------
+    def prep_block(self, x: np.ndarray, suh: np.ndarray) -> np.ndarray:
+        xt = np.empty(128, np.float32)
+        self.L.fto_prep_block(_ptr(np.ascontiguousarray(x, np.float32)), _ptr(np.ascontiguousarray(suh, np.float16)), _ptr(xt))
+        return xt
+
+    def out_block(self, y: np.ndarray, svh: np.ndarray) -> np.ndarray:
+        y = np.array(y, np.float32)
+        self.L.fto_out_block(_ptr(y), _ptr(np.ascontiguousarray(svh, np.float16)))
+        return y
+
+    # --- grouping --------------------------------------------------------------------------------------------
+    def group(self, sel: np.ndarray, w: np.ndarray, E: int):
+        sel = np.ascontiguousarray(sel, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        ntok, topk = sel.shape
+        n = max(1, ntok * topk)
+        offsets = np.zeros(E + 1, np.int32)
+        row_token = np.zeros(n, np.int32)
+        row_weight = np.zeros(n, np.float32)
+        row_pick = np.zeros(n, np.int32)
+        pick_row = np.zeros(n, np.int32)
+        P = self.L.fto_group(_ptr(sel), _ptr(w), ntok, topk, E, _ptr(offsets), _ptr(row_token), _ptr(row_weight),
+                             _ptr(row_pick), _ptr(pick_row))
+        return dict(offsets=offsets, row_token=row_token[:P], row_weight=row_weight[:P], row_pick=row_pick[:P],
+                    pick_row=pick_row[:ntok * topk], P=P)
+
+    def jobs_ref(self, sel: np.ndarray, w: np.ndarray, E: int, maxm: int = 8):
+        sel = np.ascontiguousarray(sel, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        ntok, topk = sel.shape
+        n = max(1, ntok * topk)
+        je = np.zeros(n, np.int32); jm = np.zeros(n, np.int32)
+        jt = np.zeros((n, maxm), np.int32); jw = np.zeros((n, maxm), np.float32)
+        nj = self.L.fto_jobs_ref(_ptr(sel), _ptr(w), ntok, topk, E, maxm, _ptr(je), _ptr(jm), _ptr(jt), _ptr(jw))
+        return [(int(je[j]), [int(t) for t in jt[j, :jm[j]]], [float(x) for x in jw[j, :jm[j]]]) for j in range(nj)]
+
+    # --- experts / layer -------------------------------------------------------------------------------------
+    def _expert_struct(self, bank, e: int, keep: list):
+        ex = _Expert()
+        for p in range(3):
+            t = bank.proj(e, p)
+            s = np.ascontiguousarray(bank.suh[p][e])
+            v = np.ascontiguousarray(bank.svh[p][e])
+            keep += [t, s, v]
+            ex.tr[p] = t.ctypes.data
+            ex.suh[p] = s.ctypes.data
+            ex.svh[p] = v.ctypes.data
+            ex.K[p] = bank.bits[p]
+        return ex
+
+    def expert(self, bank, e: int, x: np.ndarray, mode: int = 1, act_limit: float = 0.0) -> np.ndarray:
+        keep: list = []
+        ex = self._expert_struct(bank, e, keep)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, bank.H)
+        y = np.empty((x.shape[0], bank.H), np.float32)
+        self.L.fto_expert(C.byref(ex), bank.H, bank.I, mode, act_limit, _ptr(x), x.shape[0], _ptr(y))
+        return y
+
+    def moe_forward(self, bank, x: np.ndarray, sel: np.ndarray, w: np.ndarray, mode: int = 1,
+                    act_limit: float = 0.0, with_shared: bool | None = None) -> np.ndarray:
+        """fp32 [ntok, H] = sum over picks (pick order) of w * expert(x) (+ shared expert when the bank has one)."""
+        keep: list = []
+        exs = [self._expert_struct(bank, e, keep) for e in range(bank.E)]
+        arr = (_Expert * bank.E)(*exs)
+        shared = bank.shared if with_shared is None else with_shared
+        sh = self._expert_struct(bank, bank.E, keep) if shared else None
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, bank.H)
+        sel = np.ascontiguousarray(sel, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty((x.shape[0], bank.H), np.float32)
+        self.L.fto_moe_forward(arr, bank.E, C.byref(sh) if sh is not None else None, bank.H, bank.I, mode, act_limit,
+                               _ptr(x), x.shape[0], _ptr(sel), _ptr(w), sel.shape[1], _ptr(out))
+        return out
+
+
+class Reference:
+    """The reference's own ft_core.h through oracle/ref_shim.cpp (K=3 only, as the reference)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (needs the reference tree; run `make -C oracle ref`)")
+        L = C.CDLL(path)
+        L.ftref_init.restype = _I
+        L.ftref_set_act_limit.argtypes = [_F]
+        L.ftref_dense.argtypes = [_P, _I, _I, _P]
+        L.ftref_layer_new.restype = _P
+        L.ftref_layer_new.argtypes = [_I, _I, _I, _P, _P, _P]
+        L.ftref_layer_free.argtypes = [_P]
+        L.ftref_pool_start.restype = _I
+        L.ftref_pool_start.argtypes = [_I, _P, _I]
+        L.ftref_moe_forward.restype = _I
+        L.ftref_moe_forward.argtypes = [_P, _P, _I, _P, _P, _I, _P, _I]
+        L.ftref_moe_forward_band.restype = _I
+        L.ftref_moe_forward_band.argtypes = [_P, _P, _I, _P, _P, _I, _P, _I]
+        L.ftref_expert_fp64.argtypes = [_P, _I, _P, _P]
+        L.ftref_init()
+        self.L = L
+        self.pool_threads = 0
+
+    def dense(self, tr: np.ndarray, k: int, n: int) -> np.ndarray:
+        W = np.empty((k, n), np.float32)
+        self.L.ftref_dense(_ptr(np.ascontiguousarray(tr)), k, n, _ptr(W))
+        return W
+
+    def start_pool(self, threads: int, cpus=None):
+        if self.pool_threads:
+            return
+        cpus = list(cpus) if cpus is not None else sorted(os.sched_getaffinity(0))[:threads]
+        arr = np.array(cpus, np.int32)
+        if self.L.ftref_pool_start(threads, _ptr(arr), len(cpus)) != 0:
+            raise RuntimeError("pool already running")
+        self.pool_threads = threads
+
+    def stop_pool(self):
+        if self.pool_threads:
+            self.L.ftref_pool_stop()
+            self.pool_threads = 0
+
+    class Layer:
+        def __init__(self, ref: "Reference", bank, with_shared: bool):
+            assert all(b == 3 for b in bank.bits), "the reference is K=3 only (ft_core.h:30)"
+            n = bank.E + (1 if with_shared and bank.shared else 0)
+            self.keep = []
+            tr = (_P * (3 * n))(); su = (_P * (3 * n))(); sv = (_P * (3 * n))()
+            for e in range(n):
+                for p in range(3):
+                    t = bank.proj(e, p)
+                    s = np.ascontiguousarray(bank.suh[p][e]); v = np.ascontiguousarray(bank.svh[p][e])
+                    self.keep += [t, s, v]
+                    tr[3 * e + p] = t.ctypes.data; su[3 * e + p] = s.ctypes.data; sv[3 * e + p] = v.ctypes.data
+            self.ref = ref
+            self.E = n
+            self.H = bank.H
+            self.h = ref.L.ftref_layer_new(bank.H, bank.I, n, tr, su, sv)
+
+        def __del__(self):
+            try:
+                self.ref.L.ftref_layer_free(self.h)
+            except Exception:
+                pass
+
+    def layer(self, bank, with_shared: bool = True) -> "Reference.Layer":
+        return Reference.Layer(self, bank, with_shared)
+
+    def moe_forward(self, layer: "Reference.Layer", x: np.ndarray, sel: np.ndarray, w: np.ndarray, mode: int = 1,
+                    band: bool = False) -> np.ndarray:
+        assert mode in (0, 1), "mode 2 (I16) is invalid at H > 4096 in the reference (ft_core.h:1353)"
+        if not self.pool_threads:
+            self.start_pool(1)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, layer.H)
+        sel = np.ascontiguousarray(sel, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.zeros((x.shape[0], layer.H), np.float32)
+        fn = self.L.ftref_moe_forward_band if band else self.L.ftref_moe_forward
+        rc = fn(layer.h, _ptr(x), x.shape[0], _ptr(sel), _ptr(w), sel.shape[1], _ptr(out), mode)
+        if rc != 0:
+            raise RuntimeError(f"reference moe_forward rc={rc}")
+        return out
+
+    def expert_fp64(self, layer: "Reference.Layer", e: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(layer.H)
+        y = np.empty(layer.H, np.float32)
+        self.L.ftref_expert_fp64(layer.h, e, _ptr(x), _ptr(y))
+        return y
+
+
+def with_shared_routes(sel: np.ndarray, w: np.ndarray, E: int):
+    """Append the shared expert as pick index E with weight 1 to every token's route (how the reference arm and
+    the reference-pinned tests fold the always-on shared expert into moe_forward)."""
+    ntok = sel.shape[0]
+    sel2 = np.concatenate([sel, np.full((ntok, 1), E, np.int32)], axis=1)
+    w2 = np.concatenate([w, np.ones((ntok, 1), np.float32)], axis=1)
+    return sel2, w2
+
+
+def rel_err(a: np.ndarray, ref: np.ndarray):
+    """(max-abs / RMS(ref), rel-RMS) - the parity metrics of the tolerance max-abs <= 2e-3 x RMS(output)."""
+    a = np.asarray(a, np.float64); ref = np.asarray(ref, np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref))) or 1e-30
+    d = a - ref
+    return float(np.max(np.abs(d))) / rms, float(np.sqrt(np.mean(d * d))) / rms
