@@ -165,6 +165,7 @@ def run_reference_impl(args, rank, world):
 
 # ------------------------------------------------------------------------------------------------------------------
 def main():
+    global E
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -174,6 +175,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", default="1,8,32", help="extra decode batches measured (device time only)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")
+    ap.add_argument("--profile", action="store_true", help="device steps only (no e2e, sweep or CPU baseline): for ncu")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -184,6 +187,10 @@ def main():
     if args.impl == "reference":
         return run_reference_impl(args, rank, world)
 
+    E = args.experts
+    if args.profile:
+        args.no_cpu_baseline = True
+        args.sweep = ""
     import torch
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -270,6 +277,13 @@ def main():
     gu_gbs = sum(gu_bytes) / (sum(gu_ms) / 1e3) / 1e9
     phase_share = [sum(p[k] for p in r["phase_ms"]) / sum(step_ms) for k in range(_lib.PHASES - 1)]
 
+    if args.profile:
+        if rank == 0:
+            print(json.dumps({"profile": True, "ms_per_step": T_ms / args.steps, "gateup_gbs": gu_gbs,
+                              "layer_gbs": achieved_layer_gbs, "phase_share": phase_share}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     # ---- end to end through the public API: pinned host inputs, H2D, forward, D2H of the result ----
     routes = make_routes(B, 5000 + rank)
     x_h = torch.randn((B, H)).half().pin_memory()

@@ -107,12 +107,15 @@ struct LaneDecode
     }
 };
 
+// Shared-memory word load as an ordinary C++ load, so the compiler may schedule it freely between the (memory-
+// clobbering) mbarrier waits.
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
-// fp16 pair (lo = a, hi = b) of codebook weights from two byte sums, one fp16 rounding (hfma), ft_core.h:81-83
+// fp16 pair (lo = a, hi = b) of codebook weights from two byte sums, one fp16 rounding (hfma), ft_core.h:81-83.
+// sa, sb are 0x6400 + s (< 2^16), so the pack is an exact multiply-add (FMA pipe; the integer ALU pipe is the scarcer).
 __device__ __forceinline__ uint32_t codebook_pair(uint32_t sa, uint32_t sb)
 {
-    const uint32_t hb = __byte_perm(sa, sb, 0x5410);                // half(1024+sa) | half(1024+sb) << 16
+    const uint32_t hb = sb * 65536u + sa;                            // half(1024+sa) | half(1024+sb) << 16
     __half2 h = *reinterpret_cast<const __half2*>(&hb);
     const __half2 kinv = __halves2half2(__ushort_as_half(KINV_BITS), __ushort_as_half(KINV_BITS));
     const __half2 kbias = __halves2half2(__ushort_as_half(KBIAS_BITS), __ushort_as_half(KBIAS_BITS));
@@ -120,30 +123,62 @@ __device__ __forceinline__ uint32_t codebook_pair(uint32_t sa, uint32_t sb)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Decode lane's 8 weights of the tile at `tile` (shared memory) into the mma.m16n8k16 A fragment of W^T:
-// a[0] = (j0, j1), a[1] = (j4, j5), a[2] = (j2, j3), a[3] = (j6, j7).
+// ---- decode with the byte sums on the tensor pipe --------------------------------------------------------------------
+//
+// The 8 product words x_j = state_j * MUL1 of a lane go into two mma.m16n8k32 u8 x u8 -> s32 as A operands; B is a
+// constant 0/1 pattern selecting the 4 bytes of one word per output (B[k][n] = 1 iff k/4 == n) and C = 0x6400, so
+// D[m][n] = 0x6400 + bytesum(word (m, n)): the fp16 bit pattern of 1024 + s. Word (m, n) is slot a0 (n < 4) / a2 (n >= 4)
+// of lane (m % 8, n % 4) for m < 8, a1 / a3 for m >= 8. With IMMA #1 fed (x0, x4, x1, x5) and IMMA #2 fed
+// (x2, x6, x3, x7), lane (g, tq) receives the sums of tile positions (rows rho(2tq), rho(2tq+1) [+8 for IMMA #2],
+// columns g and g+8), rho(n) = 2n for n < 4, 2(n-4)+1 otherwise. Output columns stay the lane's own (g, g+8); the
+// tile rows arrive permuted, so the activations (B operand of the following f16 MMA) are stored with the rows of each
+// 16-row tile in the order PERM16 below: B-fragment k-slot h holds input row PERM16[h].
+//   PERM16 = {0, 2, 4, 6, 1, 3, 5, 7, 8, 10, 12, 14, 9, 11, 13, 15}
+__host__ __device__ constexpr int perm16(int h) { return (h & 8) | ((h & 4) ? (((h & 3) << 1) | 1) : ((h & 3) << 1)); }
+// position h of input row r within its 16-row tile (inverse of perm16)
+__host__ __device__ constexpr int perm16_inv(int r) { return (r & 8) | ((r & 1) ? (4 | ((r & 7) >> 1)) : ((r & 7) >> 1)); }
+
+__device__ __forceinline__ void imma_bytesum(uint32_t d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1, uint32_t c)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
+struct OnesFrag
+{
+    uint32_t b0, b1;
+    __device__ __forceinline__ void init(int lane)
+    {
+        const int g = lane >> 2, tq = lane & 3;
+        b0 = (g == tq) ? 0x01010101u : 0u;
+        b1 = (g == 4 + tq) ? 0x01010101u : 0u;
+    }
+};
+
+// Same A fragment as decode_frag but with the rows of the tile permuted by PERM16 (see above).
 template <int K>
-__device__ __forceinline__ void decode_frag(const uint8_t* tile, const LaneDecode<K>& L, uint32_t a[4])
+__device__ __forceinline__ void decode_frag_tc(const uint8_t* tile, const LaneDecode<K>& L, const OnesFrag& ones, uint32_t a[4])
 {
     const uint32_t hi = lds32(tile + L.off_hi), lo = lds32(tile + L.off_lo);
     const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
     const uint32_t hi2 = hi >> L.pre;
-    uint32_t s[8];
+    uint32_t x[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-    {
-        const uint32_t st = __funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu;
-        s[j] = __dp4a(st * MUL1, 0x01010101u, 0x6400u);              // 0x6400 + bytesum = fp16 bits of 1024 + s
-    }
-    a[0] = codebook_pair(s[0], s[1]);
-    a[1] = codebook_pair(s[4], s[5]);
-    a[2] = codebook_pair(s[2], s[3]);
-    a[3] = codebook_pair(s[6], s[7]);
+    for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
+    uint32_t d1[4], d2[4];
+    imma_bytesum(d1, x[0], x[4], x[1], x[5], ones.b0, ones.b1, 0x6400u);
+    imma_bytesum(d2, x[2], x[6], x[3], x[7], ones.b0, ones.b1, 0x6400u);
+    a[0] = codebook_pair(d1[0], d1[1]);
+    a[1] = codebook_pair(d1[2], d1[3]);
+    a[2] = codebook_pair(d2[0], d2[1]);
+    a[3] = codebook_pair(d2[2], d2[3]);
 }
 
 __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
 {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }

@@ -30,7 +30,8 @@ constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
 constexpr int XROW = 272;    // bytes per staged activation row: 128 fp16 + 16 bytes pad (conflict-free B loads)
-constexpr int RING_BYTES = 100 * 1024;
+constexpr int RING_BYTES = 64 * 1024;    // per CTA; CTAS_PER_SM rings share an SM
+constexpr int CTAS_PER_SM = 3;
 
 template <int K0, int K1, int NMAT>
 struct Cfg
@@ -68,7 +69,7 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
 
 template <int K0, int K1, int NMAT, bool GATEUP>
-__global__ void __launch_bounds__(NTHR, 1) gemv_kernel(GemvArgs a)
+__global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
 {
     using C = Cfg<K0, K1, NMAT>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -146,17 +147,25 @@ __global__ void __launch_bounds__(NTHR, 1) gemv_kernel(GemvArgs a)
     L0.init(lane);
     LaneDecode<K1> L1;
     L1.init(lane);
+    OnesFrag ones;
+    ones.init(lane);
     const int g = lane >> 2, tq = lane & 3;
+    // per-lane offsets inside a stage: this warp's tile of k-row 0 and this lane's B-fragment words
+    const int t0_off = warp * C::TB0, t1_off = C::MAT0 + warp * C::TB1;
+    const int x_off = C::MAT0 + C::MAT1 + g * XROW + tq * 4;
     long long it = 0;
     for (long long item = blockIdx.x; item < items; item += gridDim.x)
     {
-        const int ks = (int) (item % S);
         const long long jn = item / S;
         const int nbi = (int) (jn % nb), j = (int) (jn / nb);
         const int4 job = a.jobs[j];
-        float acc[NMAT][4];
+        // Accumulation: one tensor-core chain per 128-input block (a pipeline stage), then the block sum is added into
+        // a (hi, lo) fp32 pair with Fast2Sum, so rounding errors do not grow with the chain length.
+        float acc[NMAT][4], lo[NMAT][4];
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[m][v] = lo[m][v] = 0.0f;
 
         for (int q = 0; q < kqs; ++q, ++it)
         {
@@ -164,23 +173,40 @@ __global__ void __launch_bounds__(NTHR, 1) gemv_kernel(GemvArgs a)
             const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
             if (!s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(a.err, ERR_TIMEOUT_FULL); s_abort = 1; }
             const uint8_t* st = ring + s * C::STAGE;
-            const uint8_t* xs = st + C::MAT0 + C::MAT1 + g * XROW + tq * 4;
-#pragma unroll 4
+            float blk[NMAT][4];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) blk[m][0] = blk[m][1] = blk[m][2] = blk[m][3] = 0.0f;
+#pragma unroll
             for (int r = 0; r < RB; ++r)
             {
                 uint32_t af[4];
-                decode_frag<K0>(st + r * C::ROW0 + warp * C::TB0, L0, af);
-                mma16816(acc[0], af, lds32(xs + r * 32), lds32(xs + r * 32 + 16));
+                decode_frag_tc<K0>(st + t0_off + r * C::ROW0, L0, ones, af);
+                mma16816(blk[0], af, lds32(st + x_off + r * 32), lds32(st + x_off + r * 32 + 16));
                 if (NMAT > 1)
                 {
                     uint32_t bf[4];
-                    decode_frag<K1>(st + C::MAT0 + r * C::ROW1 + warp * C::TB1, L1, bf);
-                    mma16816(acc[NMAT - 1], bf, lds32(xs + C::XS + r * 32), lds32(xs + C::XS + r * 32 + 16));
+                    decode_frag_tc<K1>(st + t1_off + r * C::ROW1, L1, ones, bf);
+                    mma16816(blk[NMAT - 1], bf, lds32(st + x_off + C::XS + r * 32), lds32(st + x_off + C::XS + r * 32 + 16));
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                {
+                    const float sum = __fadd_rn(acc[m][v], blk[m][v]);
+                    const float big = fabsf(acc[m][v]) >= fabsf(blk[m][v]) ? acc[m][v] : blk[m][v];
+                    const float small = fabsf(acc[m][v]) >= fabsf(blk[m][v]) ? blk[m][v] : acc[m][v];
+                    lo[m][v] = __fadd_rn(lo[m][v], __fsub_rn(small, __fsub_rn(sum, big)));
+                    acc[m][v] = sum;
+                }
         }
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[m][v] = __fadd_rn(acc[m][v], lo[m][v]);
 
         // ---- epilogue: fragments -> red[mat][token][128] ----
 #pragma unroll
@@ -246,7 +272,10 @@ __global__ void __launch_bounds__(NTHR, 1) gemv_kernel(GemvArgs a)
                 had128_warp(av, lane);
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    a.xd[(size_t) row * a.ndim + nbi * 128 + lane + 32 * q] = __float2half_rn(__fmul_rn(av[q], HAD));
+                {
+                    const int c = lane + 32 * q;     // stored in PERM16 order inside each 16-row tile (decode_frag_tc)
+                    a.xd[(size_t) row * a.ndim + nbi * 128 + (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(av[q], HAD));
+                }
             }
             else
             {
@@ -304,7 +333,11 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
     had128_warp(v, lane);
     __half* out = (p ? a.xu : a.xg) + (size_t) row * a.H + b * 128;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) out[lane + 32 * q] = __float2half_rn(__fmul_rn(v[q], HAD));
+    for (int q = 0; q < 4; ++q)
+    {
+        const int c = lane + 32 * q;             // PERM16 order inside each 16-row tile (decode_frag_tc)
+        out[(c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
+    }
 }
 
 // ---- combine: out[t] = sum_k w * y[row(t,k)] (+ shared), fp32, pick order ----
@@ -359,28 +392,30 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
     }
 }
 
-// ---- known-answer decode of whole tiles ----
+// ---- known-answer decode of whole tiles (the GEMV's own decode_frag_tc, rows un-permuted on the way out) ----
 template <int K>
 __global__ void decode_tiles_kernel(const uint8_t* tiles, int ntiles, uint16_t* out)
 {
     __shared__ __align__(16) uint8_t tile[8][32 * 4];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + w;
-    if (t >= ntiles) return;
+    if (t >= ntiles) return;        // warp-uniform
     for (int i = lane; i < 32 * K; i += 32) tile[w][i] = tiles[(size_t) t * 32 * K + i];
     __syncwarp();
     LaneDecode<K> L;
     L.init(lane);
+    OnesFrag ones;
+    ones.init(lane);
     uint32_t a[4];
-    decode_frag<K>(tile[w], L, a);
+    decode_frag_tc<K>(tile[w], L, ones, a);
     const int g = lane >> 2, tq = lane & 3;
-    // a[0] = (j0, j1) rows 2tq, 2tq+1 col g; a[2] = (j2, j3) rows 2tq+8, 2tq+9 col g; a[1], a[3] the same at col g+8
+    // a[0] = rows (perm16(2tq), perm16(2tq+1)) of column g, a[1] the same rows of column g+8, a[2] / a[3] those rows + 8
+    const int r0 = perm16(2 * tq), r1 = perm16(2 * tq + 1);
     uint16_t* o = out + (size_t) t * 256;
-    const int r0 = 2 * tq;
-    o[(r0) * 16 + g] = a[0] & 0xffff;          o[(r0 + 1) * 16 + g] = a[0] >> 16;
-    o[(r0 + 8) * 16 + g] = a[2] & 0xffff;      o[(r0 + 9) * 16 + g] = a[2] >> 16;
-    o[(r0) * 16 + g + 8] = a[1] & 0xffff;      o[(r0 + 1) * 16 + g + 8] = a[1] >> 16;
-    o[(r0 + 8) * 16 + g + 8] = a[3] & 0xffff;  o[(r0 + 9) * 16 + g + 8] = a[3] >> 16;
+    o[r0 * 16 + g] = a[0] & 0xffff;             o[r1 * 16 + g] = a[0] >> 16;
+    o[r0 * 16 + g + 8] = a[1] & 0xffff;         o[r1 * 16 + g + 8] = a[1] >> 16;
+    o[(r0 + 8) * 16 + g] = a[2] & 0xffff;       o[(r1 + 8) * 16 + g] = a[2] >> 16;
+    o[(r0 + 8) * 16 + g + 8] = a[3] & 0xffff;   o[(r1 + 8) * 16 + g + 8] = a[3] >> 16;
 }
 
 template <int K0, int K1, int NMAT, bool GATEUP>
@@ -442,7 +477,7 @@ int gemv_grid_ctas(const Layer& L)
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, L.device) != cudaSuccess || v <= 0) v = 148;
         sms[L.device] = v;
     }
-    return sms[L.device];   // one CTA (9 warps, ~100 KB ring) per SM
+    return sms[L.device] * CTAS_PER_SM;   // CTAS_PER_SM CTAs (9 warps, <= 64 KB ring each) per SM
 }
 
 WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)

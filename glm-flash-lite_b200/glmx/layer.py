@@ -155,6 +155,9 @@ class MoELayer:
         ws = self.workspace(ntok, topk)
         ev = None
         if events is not None:
+            for e in events:
+                if e is not None and not e.cuda_event:
+                    e.record(stream if stream is not None else torch.cuda.current_stream())   # creates the event
             ev = (C.c_void_p * _lib.PHASES)(*[e.cuda_event if e is not None else 0 for e in events])
         check(self.lib.glmx_moe_forward_timed(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
                                               _dt(w), topk, int(mode), out.data_ptr(), _dt(out), int(bool(accumulate)),

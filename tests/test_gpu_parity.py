@@ -45,7 +45,9 @@ def test_route_bit_exact(oracle, dev, ntok, topk, E):
     bank = synth.make_bank(128, 128, E, shared=True, seed=1)
     layer = _layer(bank, dev)
     rng = np.random.default_rng(ntok * 7 + E)
-    sel = np.stack([rng.permutation(E)[:topk] for _ in range(ntok)]).astype(np.int32).reshape(ntok, topk)
+    sel = np.zeros((ntok, topk), np.int32)
+    for t in range(ntok):
+        sel[t] = rng.permutation(E)[:topk]
     if ntok:
         sel[rng.random(sel.shape) < 0.03] = -1
         sel[rng.random(sel.shape) < 0.01] = E + 3        # out of range: skipped like sel < 0
