@@ -177,6 +177,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")
     ap.add_argument("--profile", action="store_true", help="device steps only (no e2e, sweep or CPU baseline): for ncu")
+    ap.add_argument("--mode", type=int, default=2, choices=[1, 2], help="1 EXACT (fp16 weights, fp32 tensor-core sums), "
+                    "2 I16 (int16 activations, exact integer tensor-core sums; bit-identical to the reference's I16 mode)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -229,7 +231,7 @@ def main():
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_l2 else None
         ph = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.PHASES)] for _ in range(steps)]
         for i in range(warmup):
-            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out)
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, mode=args.mode)
         if dist:
             dist.barrier()
         torch.cuda.synchronize(dev)
@@ -239,7 +241,7 @@ def main():
         for i in range(steps):
             if flush is not None:
                 flush.zero_()
-            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, events=ph[i])
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, events=ph[i], mode=args.mode)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if dist:
@@ -297,7 +299,7 @@ def main():
     def e2e_step(i):
         x_d.copy_(x_h, non_blocking=True); s_d.copy_(sel_h[i % ROUTE_POOL], non_blocking=True)
         w_d.copy_(w_h[i % ROUTE_POOL], non_blocking=True)
-        layer.forward(x_d, s_d, w_d, out=o_d)
+        layer.forward(x_d, s_d, w_d, out=o_d, mode=args.mode)
         out_h.copy_(o_d, non_blocking=True)
     for i in range(args.warmup):
         e2e_step(i)
@@ -355,9 +357,9 @@ def main():
     line = {
         "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16-weights/fp32-acc", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
         "config": {"workload": f"configs[1] decode MoE layer B={B} (288 routed + 1 shared, H=6144, I=1536, K=3, top-8)",
-                   "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": "EXACT",
+                   "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": {1: "EXACT", 2: "I16"}[args.mode],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (touched trellis per step > 126 MB)" if B >= 32 else "L2 flushed between steps",
                    "unique_experts_per_step": statistics.mean(r["uniq"])},

@@ -150,8 +150,8 @@ int glmx_route(const glmx_layer* l, const void* sel, int sel_dtype, const void* 
     int rc = check_common(l, ntok, topk, sel_dtype, w_dtype, ws, ws_bytes, &lay, &grid, "glmx_route");
     if (rc) return rc;
     if (ntok * topk > 0 && (!sel || !w)) return fail(GLMX_E_ARG, "glmx_route: null sel/w");
-    cudaError_t e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, static_cast<uint8_t*>(ws), lay, grid,
-                                 static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, MAXM, static_cast<uint8_t*>(ws), lay,
+                                 grid, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "glmx_route: launch");
     return GLMX_OK;
 }
@@ -172,7 +172,8 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     int grid;
     int rc = check_common(l, ntok, topk, sel_dtype, w_dtype, ws, ws_bytes, &lay, &grid, "glmx_moe_forward");
     if (rc) return rc;
-    if (mode != GLMX_MODE_EXACT) return fail(GLMX_E_ARG, "glmx_moe_forward: mode must be GLMX_MODE_EXACT (1)");
+    if (mode != GLMX_MODE_EXACT && mode != GLMX_MODE_I16)
+        return fail(GLMX_E_ARG, "glmx_moe_forward: mode must be GLMX_MODE_EXACT (1) or GLMX_MODE_I16 (2)");
     if (x_dtype != GLMX_F16 && x_dtype != GLMX_F32 && x_dtype != GLMX_BF16)
         return fail(GLMX_E_ARG, "glmx_moe_forward: x dtype must be fp16, fp32 or bf16");
     if (out_dtype != GLMX_F16 && out_dtype != GLMX_F32) return fail(GLMX_E_ARG, "glmx_moe_forward: out dtype must be fp16 or fp32");
@@ -183,10 +184,14 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     cudaError_t e = cudaSuccess;
     if (events && events[0]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[0]), st);
-    if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, wsb, lay, grid, st);
+    const int maxm = mode == GLMX_MODE_I16 ? I16_MAXM : MAXM;
+    if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, maxm, wsb, lay, grid, st);
     if (e == cudaSuccess && events && events[1]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[1]), st);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: route launch");
-    e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, mode, out, out_dtype, accumulate, wsb, lay, grid, st, events);
+    if (mode == GLMX_MODE_I16)
+        e = launch_i16_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events);
+    else
+        e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, mode, out, out_dtype, accumulate, wsb, lay, grid, st, events);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: launch");
     return GLMX_OK;
 }

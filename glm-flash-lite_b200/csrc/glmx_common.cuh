@@ -157,16 +157,32 @@ struct OnesFrag
     }
 };
 
-// Same A fragment as decode_frag but with the rows of the tile permuted by PERM16 (see above).
+// The 8 product words x_j = state_j * MUL1 (mod 2^32) of lane's stream weights 8*lane .. 8*lane+7 of a tile; the
+// codebook value of weight j is a function of bytesum(x_j) (ft_core.h:75-83).
 template <int K>
-__device__ __forceinline__ void decode_frag_tc(const uint8_t* tile, const LaneDecode<K>& L, const OnesFrag& ones, uint32_t a[4])
+__device__ __forceinline__ void decode_words(const uint8_t* tile, const LaneDecode<K>& L, uint32_t x[8])
 {
     const uint32_t hi = lds32(tile + L.off_hi), lo = lds32(tile + L.off_lo);
     const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
     const uint32_t hi2 = hi >> L.pre;
-    uint32_t x[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
+}
+
+// mma.m16n8k32, A = product bytes (u8), B = activation planes (s8), exact int32 accumulation
+__device__ __forceinline__ void imma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Same A fragment as decode_frag but with the rows of the tile permuted by PERM16 (see above).
+template <int K>
+__device__ __forceinline__ void decode_frag_tc(const uint8_t* tile, const LaneDecode<K>& L, const OnesFrag& ones, uint32_t a[4])
+{
+    uint32_t x[8];
+    decode_words<K>(tile, L, x);
     uint32_t d1[4], d2[4];
     imma_bytesum(d1, x[0], x[4], x[1], x[5], ones.b0, ones.b1, 0x6400u);
     imma_bytesum(d2, x[2], x[6], x[3], x[7], ones.b0, ones.b1, 0x6400u);

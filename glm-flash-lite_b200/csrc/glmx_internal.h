@@ -37,10 +37,12 @@ struct Plan
 // Workspace layout of one forward call (byte offsets from the workspace base, 256-byte aligned).
 struct WsLayout
 {
-    size_t plan, err, offsets, row_token, row_expert, row_pick, row_weight, pick_row, jobs;
+    size_t plan, err, offsets, row_token, row_expert, row_pick, row_weight, pick_row, jobs, row_job;
     size_t cnt_gu, cnt_d, xg, xu, xd, yrow, partials;
+    // I16 mode
+    size_t actb_gu, sc_gu, psum_gu, yraw_gu, actb_d, sc_d, psum_d;
     size_t total;
-    int rows_max, jobs_max, part_slots;
+    int rows_max, jobs_max, jobs_max_i16, part_slots;
 };
 
 WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas);
@@ -52,10 +54,15 @@ void set_error(const std::string& msg);
 
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
-                         uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);
+                         int maxm, uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);
 cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,
                                   int out_dtype, int accumulate, uint8_t* ws, const WsLayout& lay, int grid_ctas,
                                   cudaStream_t st, void* const* events);
+cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
+                               int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events);
 cudaError_t launch_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, cudaStream_t st);
+
+constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
+constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
 
 }  // namespace glmx

@@ -499,6 +499,7 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.row_weight = take(sizeof(float) * (size_t) rows);
     w.pick_row = take(sizeof(int) * (size_t) n);
     w.jobs = take(sizeof(int4) * (size_t) jobs);
+    w.row_job = take(sizeof(int) * (size_t) rows);
     w.cnt_gu = take(sizeof(int) * (size_t) jobs * (L.I / 128));
     w.cnt_d = take(sizeof(int) * (size_t) jobs * (L.H / 128));
     w.xg = take(sizeof(__half) * (size_t) rows * L.H);
@@ -506,6 +507,17 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.xd = take(sizeof(__half) * (size_t) rows * L.I);
     w.yrow = take(sizeof(float) * (size_t) rows * L.H);
     w.partials = take(sizeof(float) * (size_t) w.part_slots * 2 * MAXM * 128 + 0 * nmax);
+    // I16 mode: jobs of <= I16_MAXM rows of one expert: at most rows/4 + one partial job per expert
+    const int ji = rows < (rows + 3) / 4 + L.E_total ? rows : (rows + 3) / 4 + L.E_total;
+    w.jobs_max_i16 = ji;
+    const int BH = L.H / 128, BI = L.I / 128;
+    w.actb_gu = take((size_t) ji * 2 * BH * I16_ACT_BYTES);
+    w.sc_gu = take(sizeof(float) * 4 * (size_t) ji * 2 * BH);
+    w.psum_gu = take(sizeof(float) * (size_t) rows * 2 * BH);
+    w.yraw_gu = take(sizeof(float) * (size_t) rows * 2 * L.I);
+    w.actb_d = take((size_t) ji * BI * I16_ACT_BYTES);
+    w.sc_d = take(sizeof(float) * 4 * (size_t) ji * BI);
+    w.psum_d = take(sizeof(float) * (size_t) rows * BI);
     w.total = o;
     return w;
 }

@@ -28,11 +28,12 @@ struct RouteArgs
     const void* sel; int sel_i64;
     const void* w; int w_dtype;
     int ntok, topk, E, has_shared;
+    int maxm;                 // rows per job (8 EXACT, 4 I16)
     int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
     int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
     int grid_ctas, part_slots;
     Plan* plan;
-    int* offsets; int* row_token; int* row_expert; int* row_pick; float* row_weight; int* pick_row; int4* jobs;
+    int* offsets; int* row_token; int* row_expert; int* row_pick; float* row_weight; int* pick_row; int4* jobs; int* row_job;
     int* cnt_gu; int* cnt_d; int* err;
 };
 
@@ -121,19 +122,30 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
     const int c = tid < E ? cnt[tid] : 0;
     int P;
     const int off = block_exclusive_scan(c, warp_sums, &P);
-    const int nj = (c + MAXM - 1) / MAXM;
+    const int maxm = a.maxm;
+    const int nj = (c + maxm - 1) / maxm;
     int Jr;
     const int joff = block_exclusive_scan(nj, warp_sums, &Jr);
     if (tid < E)
     {
         a.offsets[tid] = off;
         base[tid] = off;
-        for (int q = 0; q < nj; ++q) a.jobs[joff + q] = make_int4(tid, off + q * MAXM, min(MAXM, c - q * MAXM), 0);
+        for (int q = 0; q < nj; ++q)
+        {
+            const int r0 = off + q * maxm, m = min(maxm, c - q * maxm);
+            a.jobs[joff + q] = make_int4(tid, r0, m, 0);
+            for (int i = 0; i < m; ++i) a.row_job[r0 + i] = joff + q;
+        }
     }
     if (tid == 0) a.offsets[E] = P;
     const int nsh = a.has_shared ? a.ntok : 0;
-    const int Jsh = (nsh + MAXM - 1) / MAXM;
-    for (int q = tid; q < Jsh; q += RT) a.jobs[Jr + q] = make_int4(E, P + q * MAXM, min(MAXM, nsh - q * MAXM), 0);
+    const int Jsh = (nsh + maxm - 1) / maxm;
+    for (int q = tid; q < Jsh; q += RT)
+    {
+        const int r0 = P + q * maxm, m = min(maxm, nsh - q * maxm);
+        a.jobs[Jr + q] = make_int4(E, r0, m, 0);
+        for (int i = 0; i < m; ++i) a.row_job[r0 + i] = Jr + q;
+    }
     for (int t = tid; t < nsh; t += RT)
     {
         a.row_token[P + t] = t; a.row_expert[P + t] = E; a.row_pick[P + t] = -1; a.row_weight[P + t] = 1.0f;
@@ -193,9 +205,10 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
 }  // namespace
 
 cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
-                         uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st)
+                         int maxm, uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st)
 {
     RouteArgs a;
+    a.maxm = maxm;
     a.sel = sel; a.sel_i64 = sel_i64; a.w = w; a.w_dtype = w_dtype;
     a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared;
     a.nb_gu = L.I / 128; a.nb_d = L.H / 128; a.kq_gu = L.H / 128; a.kq_d = L.I / 128;
@@ -209,6 +222,7 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
     a.row_weight = reinterpret_cast<float*>(ws + lay.row_weight);
     a.pick_row = reinterpret_cast<int*>(ws + lay.pick_row);
     a.jobs = reinterpret_cast<int4*>(ws + lay.jobs);
+    a.row_job = reinterpret_cast<int*>(ws + lay.row_job);
     a.cnt_gu = reinterpret_cast<int*>(ws + lay.cnt_gu);
     a.cnt_d = reinterpret_cast<int*>(ws + lay.cnt_d);
     a.err = reinterpret_cast<int*>(ws + lay.err);

@@ -40,6 +40,8 @@ extern "C" {
 
 /* numeric modes, same numbering as the reference's moe_forward (kernels/cpu_avx2/ft_core.h:822-823) */
 #define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights (GPU-exact), fp32 tensor-core accumulation */
+#define GLMX_MODE_I16 2     /* int16 activations per 128-block, exact integer tensor-core sums, the reference's fp32
+                               flush order (ft_core.h:418-598): bit-identical to the reference's I16 mode */
 
 typedef struct glmx_layer glmx_layer;
 
@@ -72,7 +74,7 @@ GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
 GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk);
 
 /* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
- * (expert, token), pick -> row map, jobs of <= 8 rows). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
+ * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward in I16 mode uses jobs of <= 4 rows). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
  * kernels/k110/ft_split_fast.cu:200-235) and the job grouping of moe_forward (kernels/cpu_avx2/ft_core.h:1344-1349).
  * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64); ids outside [0, E) are skipped.
  * w: device [ntok, topk] fp32 / fp16 / bf16. */

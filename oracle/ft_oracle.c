@@ -163,6 +163,118 @@ void fto_expert(const fto_expert_t* ex, int H, int I, int mode, float act_limit,
     free(g); free(u);
 }
 
+/* ---- I16 mode ---------------------------------------------------------------------------------------------- */
+
+/* ft_core.h:583-598 quant_block_i16 (values only; the reference's duplicated/permuted register layout is not needed) */
+static float quant_block_i16(const float* xt, int32_t* xi, float* sum)
+{
+    float amax = 0.0f;
+    for (int r = 0; r < 128; ++r) { const float a = fabsf(xt[r]); amax = amax < a ? a : amax; }
+    const float sc = amax > 0 ? amax / 16383.0f : 1.0f, rs = 1.0f / sc;
+    long long si = 0;
+    for (int r = 0; r < 128; ++r) { const float v = xt[r] * rs; xi[r] = (int32_t) nearbyintf(v); si += xi[r]; }
+    const float add = (float) si * sc;
+    *sum = *sum + add;
+    return sc;
+}
+
+/* byte sums of a native-layout tensor [k][n] */
+static void dense_bytesum(const uint8_t* tr, int K, int k, int n, uint16_t* S)
+{
+    fto_init();
+    const int tn = n / 16, tb = 32 * K;
+    for (int tk = 0; tk < k / 16; ++tk)
+        for (int t = 0; t < tn; ++t) {
+            const uint8_t* tile = tr + ((size_t) tk * tn + t) * tb;
+            for (int i = 0; i < 256; ++i) {
+                const int rc = PERM[i];
+                S[(size_t) (tk * 16 + rc / 16) * n + t * 16 + rc % 16] = BYTESUM[fto_state(tile, K, i)];
+            }
+        }
+}
+
+/* ft_core.h:497-541 gemv_block_i16 for all output columns of one token: xi [k] int16 values, sc [k/128] */
+static void gemv_i16(const uint16_t* S, int k, int n, const int32_t* xi, const float* sc, float sumx, float* y)
+{
+    static const int off[4] = { 0, 1, 8, 9 };
+    float* acc = (float*) calloc((size_t) n * 4, sizeof(float));
+    long long* blk = (long long*) malloc(sizeof(long long) * (size_t) n * 4);
+    for (int b = 0; b < k / 128; ++b) {
+        for (size_t i = 0; i < (size_t) n * 4; ++i) blk[i] = 0;
+        for (int tk = b * 8; tk < b * 8 + 8; ++tk)
+            for (int cl = 0; cl < 4; ++cl)
+                for (int q = 0; q < 4; ++q) {
+                    const int row = tk * 16 + 2 * q + off[cl];
+                    const long long xv = xi[row];
+                    const uint16_t* Sr = S + (size_t) row * n;
+                    for (int c = 0; c < n; ++c) blk[(size_t) c * 4 + cl] += (long long) Sr[c] * xv;
+                }
+        for (int c = 0; c < n; ++c)
+            for (int cl = 0; cl < 4; ++cl) {
+                float* a = &acc[(size_t) c * 4 + cl];
+                *a = fmaf((float) (int32_t) blk[(size_t) c * 4 + cl], sc[b], *a);
+            }
+    }
+    const float kinv = KINV, caff = 1024.0f * KINV + KBIAS;
+    for (int c = 0; c < n; ++c) {
+        const float* a = &acc[(size_t) c * 4];
+        const float lo = (a[0] + a[1]) + (a[2] + a[3]);
+        const float t0 = kinv * lo, t1 = caff * sumx;
+        y[c] = t0 + t1;
+    }
+    free(blk); free(acc);
+}
+
+void fto_expert_i16(const fto_expert_t* ex, int H, int I, float act_limit, const float* x, int m, float* y)
+{
+    fto_init();
+    uint16_t* Sg = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * I);
+    uint16_t* Su = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * I);
+    uint16_t* Sd = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) I * H);
+    dense_bytesum(ex->tr[0], ex->K[0], H, I, Sg);
+    dense_bytesum(ex->tr[1], ex->K[1], H, I, Su);
+    dense_bytesum(ex->tr[2], ex->K[2], I, H, Sd);
+    const int BH = H / 128, BI = I / 128;
+    int32_t* xg = (int32_t*) malloc(sizeof(int32_t) * (size_t) H);
+    int32_t* xu = (int32_t*) malloc(sizeof(int32_t) * (size_t) H);
+    int32_t* xd = (int32_t*) malloc(sizeof(int32_t) * (size_t) I);
+    float* scg = (float*) malloc(sizeof(float) * (size_t) BH);
+    float* scu = (float*) malloc(sizeof(float) * (size_t) BH);
+    float* scd = (float*) malloc(sizeof(float) * (size_t) BI);
+    float* sdb = (float*) malloc(sizeof(float) * (size_t) BI);
+    float* g = (float*) malloc(sizeof(float) * (size_t) I);
+    float* u = (float*) malloc(sizeof(float) * (size_t) I);
+    float xt[128];
+    for (int t = 0; t < m; ++t) {
+        const float* xr = x + (size_t) t * H;
+        float sg = 0.0f, su = 0.0f;                    /* ft_core.h:886-897 phase 0 */
+        for (int b = 0; b < BH; ++b) {
+            fto_prep_block(xr + b * 128, ex->suh[0] + b * 128, xt);
+            scg[b] = quant_block_i16(xt, xg + b * 128, &sg);
+            fto_prep_block(xr + b * 128, ex->suh[1] + b * 128, xt);
+            scu[b] = quant_block_i16(xt, xu + b * 128, &su);
+        }
+        gemv_i16(Sg, H, I, xg, scg, sg, g);            /* phase 1 (ft_core.h:899-955) */
+        gemv_i16(Su, H, I, xu, scu, su, u);
+        for (int b = 0; b < BI; ++b) {
+            fto_out_block(g + b * 128, ex->svh[0] + b * 128);
+            fto_out_block(u + b * 128, ex->svh[1] + b * 128);
+            float a[128];
+            for (int r = 0; r < 128; ++r) a[r] = r16(fto_act_mul(g[b * 128 + r], u[b * 128 + r], act_limit));
+            fto_prep_block(a, ex->suh[2] + b * 128, xt);
+            float s = 0.0f;
+            scd[b] = quant_block_i16(xt, xd + b * 128, &s);
+            sdb[b] = s;
+        }
+        float sd = 0.0f;                                /* phase 2 (ft_core.h:997-1003): block sums in order */
+        for (int b = 0; b < BI; ++b) sd = sd + sdb[b];
+        float* yr = y + (size_t) t * H;
+        gemv_i16(Sd, I, H, xd, scd, sd, yr);
+        for (int b = 0; b < BH; ++b) fto_out_block(yr + b * 128, ex->svh[2] + b * 128);
+    }
+    free(u); free(g); free(sdb); free(scd); free(scu); free(scg); free(xd); free(xu); free(xg); free(Sd); free(Su); free(Sg);
+}
+
 /* Expert-major grouping: rows sorted by (expert asc, pick index asc). Within an expert the pick index order
  * is token order, which is the order ft_core.h:1344-1349 appends tokens to an expert's jobs. */
 int fto_group(const int32_t* sel, const float* w, int ntok, int topk, int E,
@@ -218,12 +330,14 @@ void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* sha
         const int r0 = offsets[e], m = offsets[e + 1] - r0;
         if (!m) continue;
         for (int i = 0; i < m; ++i) memcpy(xs + (size_t) i * H, x + (size_t) row_token[r0 + i] * H, sizeof(float) * H);
-        fto_expert(&experts[e], H, I, mode, act_limit, xs, m, yrow + (size_t) r0 * H);
+        if (mode == 2) fto_expert_i16(&experts[e], H, I, act_limit, xs, m, yrow + (size_t) r0 * H);
+        else fto_expert(&experts[e], H, I, mode, act_limit, xs, m, yrow + (size_t) r0 * H);
     }
     float* ysh = NULL;
     if (shared && ntok) {
         ysh = (float*) malloc(sizeof(float) * (size_t) ntok * H);
-        fto_expert(shared, H, I, mode, act_limit, x, ntok, ysh);
+        if (mode == 2) fto_expert_i16(shared, H, I, act_limit, x, ntok, ysh);
+        else fto_expert(shared, H, I, mode, act_limit, x, ntok, ysh);
     }
     for (int t = 0; t < ntok; ++t) {
         float* o = out + (size_t) t * H;

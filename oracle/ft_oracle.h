@@ -71,8 +71,18 @@ int fto_group(const int32_t* sel, const float* w, int ntok, int topk, int E,
 int fto_jobs_ref(const int32_t* sel, const float* w, int ntok, int topk, int E, int maxm,
                  int32_t* job_e, int32_t* job_m, int32_t* job_tok, float* job_w);
 
+/* I16 mode (the reference's mode 2, ft_core.h:418-598): per 128-input block the transformed activations are quantised
+ * to int16 with scale amax / 16383 (quant_block_i16, ft_core.h:583-598); each output column keeps four fp32
+ * accumulators, one per tile-row class {0,2,4,6}, {1,3,5,7}, {8,10,12,14}, {9,11,13,15} (the four AVX lanes of
+ * tile_accum_i16), each fed once per block with fma(float(exact int32 block sum of bytesum * xi), scale, acc)
+ * (gemv_block_i16, ft_core.h:497-541); out = KINV * ((a0 + a1) + (a2 + a3)) + CAFF * sumx. Weights are unrounded
+ * codebook values (AFFINE). Same algorithm as the reference at any H; the reference's own scratch is sized for
+ * H / 128 <= 32 blocks (ft_core.h:1353), this restatement is not. */
+void fto_expert_i16(const fto_expert_t* ex, int H, int I, float act_limit, const float* x, int m, float* y);
+
 /* Whole layer: out[t] = sum over token t's picks in pick order of w * expert(x[t]) (fp32, ft_core.h:1020-1033
  * with the sum taken in pick order), plus the shared expert (weight 1) when shared != NULL. */
+/* mode 0 AFFINE, 1 EXACT (fp64 accumulation), 2 I16 */
 void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* shared, int H, int I, int mode,
                      float act_limit, const float* x, int ntok, const int32_t* sel, const float* w, int topk, float* out);
 

@@ -64,6 +64,7 @@ class Oracle:
         L.fto_jobs_ref.restype = _I
         L.fto_jobs_ref.argtypes = [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]
         L.fto_moe_forward.argtypes = [_P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P, _I, _P]
+        L.fto_expert_i16.argtypes = [_P, _I, _I, _F, _P, _I, _P]
         L.fto_init()
         self.L = L
 
@@ -141,6 +142,14 @@ class Oracle:
         x = np.ascontiguousarray(x, np.float32).reshape(-1, bank.H)
         y = np.empty((x.shape[0], bank.H), np.float32)
         self.L.fto_expert(C.byref(ex), bank.H, bank.I, mode, act_limit, _ptr(x), x.shape[0], _ptr(y))
+        return y
+
+    def expert_i16(self, bank, e: int, x: np.ndarray, act_limit: float = 0.0) -> np.ndarray:
+        keep: list = []
+        ex = self._expert_struct(bank, e, keep)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, bank.H)
+        y = np.empty((x.shape[0], bank.H), np.float32)
+        self.L.fto_expert_i16(C.byref(ex), bank.H, bank.I, act_limit, _ptr(x), x.shape[0], _ptr(y))
         return y
 
     def moe_forward(self, bank, x: np.ndarray, sel: np.ndarray, w: np.ndarray, mode: int = 1,
@@ -231,7 +240,8 @@ class Reference:
 
     def moe_forward(self, layer: "Reference.Layer", x: np.ndarray, sel: np.ndarray, w: np.ndarray, mode: int = 1,
                     band: bool = False) -> np.ndarray:
-        assert mode in (0, 1), "mode 2 (I16) is invalid at H > 4096 in the reference (ft_core.h:1353)"
+        assert mode in (0, 1) or (mode == 2 and layer.H <= 4096), \
+            "mode 2 (I16) is invalid at H > 4096 in the reference (scratch sized for 32 blocks, ft_core.h:1353)"
         if not self.pool_threads:
             self.start_pool(1)
         x = np.ascontiguousarray(x, np.float32).reshape(-1, layer.H)

@@ -83,6 +83,25 @@ def main():
             names.append(tag)
         d["cases"] = np.array(names)
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **d)
+    # 3. I16 mode (the reference's mode 2) at the reference's own geometry H=4096, I=2048, where its scratch is valid
+    #    (ft_core.h:1353). Single-pick routes (weight 1) make the layer output equal one expert's output, so the pin is
+    #    bit-exact; a multi-pick case checks the combine.
+    H, I, E, seed = 4096, 2048, 5, 404
+    b = bank_splitmix(H, I, E, False, seed)
+    d = {}
+    save_bank("", b, seed, d)
+    L = ref.layer(b, with_shared=False)
+    rng = np.random.default_rng(4242)
+    x = (0.35 * rng.standard_normal((E, H))).astype(np.float16).astype(np.float32)
+    sel = np.arange(E, dtype=np.int32).reshape(E, 1)
+    w = np.ones((E, 1), np.float32)
+    d["single_x"] = x; d["single_sel"] = sel; d["single_w"] = w
+    d["single_i16"] = ref.moe_forward(L, x, sel, w, mode=2)
+    sel2 = np.array([[(t + 2 * k) % E for k in range(3)] for t in range(3)], np.int32)
+    w2 = np.array([[0.5, 0.3, 0.2]] * 3, np.float32)
+    d["multi_x"] = x[:3]; d["multi_sel"] = sel2; d["multi_w"] = w2
+    d["multi_i16"] = ref.moe_forward(L, x[:3], sel2, w2, mode=2)
+    np.savez_compressed(os.path.join(HERE, "moe_i16_h4096.npz"), **d)
     ref.stop_pool()
     print("golden fixtures written to", HERE)
 

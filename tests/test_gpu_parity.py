@@ -139,3 +139,49 @@ def test_accumulate_and_fp16_out(oracle, dev):
     torch.testing.assert_close(acc, base + plain, rtol=0, atol=1e-6)
     h = layer.forward(xt, st, wt, out_dtype=torch.float16)
     torch.testing.assert_close(h.float(), plain.half().float(), rtol=0, atol=0)
+
+
+# ---- I16 mode: bit-exact ---------------------------------------------------------------------------------------------
+
+def test_i16_golden_reference_bit_exact(dev):
+    """GPU I16 mode vs the reference's own moe_forward mode 2 at its geometry (H=4096, I=2048): bit-identical."""
+    d = load_golden("moe_i16_h4096")
+    bank = golden_bank(d)
+    layer = _layer(bank, dev)
+    x, sel, w = (torch.from_numpy(d[k]).to(dev) for k in ("single_x", "single_sel", "single_w"))
+    got = layer.forward(x, sel, w, mode=2).cpu().numpy()
+    assert layer.check_device(*sel.shape) == 0
+    np.testing.assert_array_equal(got, d["single_i16"])
+    x, sel, w = (torch.from_numpy(d[k]).to(dev) for k in ("multi_x", "multi_sel", "multi_w"))
+    got = layer.forward(x, sel, w, mode=2).cpu().numpy()
+    mx, rr = parity(got, d["multi_i16"])
+    assert mx < 1e-6 and rr < 1e-7, (mx, rr)
+
+
+@pytest.mark.parametrize("ntok,E,topk", [(1, 24, 8), (5, 24, 8), (16, 40, 8)])
+def test_i16_baseline_geometry_bit_exact(oracle, dev, ntok, E, topk):
+    """BASELINE geometry (H=6144, I=1536, K=3) with a shared expert: GPU I16 == oracle I16 restatement, every bit."""
+    from glmx import synth
+    bank = synth.make_bank(6144, 1536, E, shared=True, seed=131 + ntok)
+    layer = _layer(bank, dev)
+    x = synth.make_x(ntok, 6144, 141 + ntok)
+    sel, w = synth.route_uniform(ntok, E, topk, 151 + ntok)
+    got = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(sel).to(dev), torch.from_numpy(w).to(dev),
+                        mode=2).cpu().numpy()
+    want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=2)
+    mx, rr = parity(got, want)
+    assert mx <= TOL_MAXABS_REL_RMS, (mx, rr)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("bits", [(2, 2, 2), (4, 4, 4), (2, 3, 4)])
+def test_i16_mixed_bitrate_bit_exact(oracle, dev, bits):
+    from glmx import synth
+    E = 6
+    bank = synth.make_bank(1024, 512, E, shared=True, bits=bits, seed=161)
+    layer = _layer(bank, dev)
+    x = synth.make_x(6, 1024, 171)
+    sel, w = synth.route_uniform(6, E, 4, 181)
+    got = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(sel).to(dev), torch.from_numpy(w).to(dev),
+                        mode=2).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=2))

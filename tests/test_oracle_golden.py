@@ -72,3 +72,16 @@ def test_grouping_matches_reference_jobs(oracle):
                 assert r == -1
             else:
                 assert g["row_pick"][r] == p and g["row_token"][r] == p // topk
+
+
+def test_i16_restatement_bit_exact_vs_reference(oracle):
+    """The I16 restatement equals the reference's own mode 2 (moe_forward, ft_core.h) bit for bit on single-pick
+    routes (layer output = one expert's output) and up to the combine's summation order on multi-pick routes."""
+    d = load_golden("moe_i16_h4096")
+    b = golden_bank(d)
+    x, sel = d["single_x"], d["single_sel"]
+    for t in range(x.shape[0]):
+        np.testing.assert_array_equal(oracle.expert_i16(b, int(sel[t, 0]), x[t])[0], d["single_i16"][t])
+    got = oracle.moe_forward(b, d["multi_x"], d["multi_sel"], d["multi_w"], mode=2)
+    mx, rr = parity(got, d["multi_i16"])
+    assert mx < 1e-6 and rr < 1e-7, (mx, rr)
