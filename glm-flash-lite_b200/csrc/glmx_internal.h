@@ -6,7 +6,7 @@
 
 #include <string>
 
-#include "../../include/glmx.h"
+#include "glmx.h"
 
 namespace glmx {
 

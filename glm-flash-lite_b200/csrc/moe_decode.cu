@@ -30,8 +30,11 @@ constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
 constexpr int XROW = 272;    // bytes per staged activation row: 128 fp16 + 16 bytes pad (conflict-free B loads)
-constexpr int RING_BYTES = 64 * 1024;    // per CTA; CTAS_PER_SM rings share an SM
-constexpr int CTAS_PER_SM = 3;
+#ifndef GLMX_EXACT_CTAS
+#define GLMX_EXACT_CTAS 3
+#endif
+constexpr int CTAS_PER_SM = GLMX_EXACT_CTAS;
+constexpr int RING_BYTES = (CTAS_PER_SM >= 3 ? 64 : 96) * 1024;    // per CTA; CTAS_PER_SM rings share an SM
 
 template <int K0, int K1, int NMAT>
 struct Cfg

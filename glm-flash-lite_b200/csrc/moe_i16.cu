@@ -30,8 +30,11 @@ namespace {
 constexpr int RB = 8;                  // tile rows per stage = one 128-input block
 constexpr int NW = 8;                  // consumer warps = 16-column n-tiles per item (128 columns)
 constexpr int NTHR = (NW + 1) * 32;
-constexpr int RING = 64 * 1024;
-constexpr int CTAS = 3;
+#ifndef GLMX_I16_CTAS
+#define GLMX_I16_CTAS 3
+#endif
+constexpr int CTAS = GLMX_I16_CTAS;                 // CTAs per SM
+constexpr int RING = (CTAS >= 3 ? 64 : 96) * 1024;   // ring bytes per CTA
 
 template <int K0, int K1, int NMAT>
 struct CfgI
@@ -201,7 +204,16 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
             {
                 const float* ps = a.psum + ((size_t) row * NMAT + m) * nkb;
                 float sumx = 0.0f;
-                for (int kb = 0; kb < nkb; ++kb) sumx = __fadd_rn(sumx, ps[kb]);
+                // the loads are independent: fetch 8 at a time, then fold them in block order
+                for (int kb0 = 0; kb0 < nkb; kb0 += 8)
+                {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = kb0 + u < nkb ? __ldg(ps + kb0 + u) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (kb0 + u < nkb) sumx = __fadd_rn(sumx, v[u]);
+                }
                 const float t1 = __fmul_rn(caff, sumx);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)

@@ -7,10 +7,11 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
-LIB_PATH = os.path.join(PKG, "lib", "libglmx.so")
+LIB_PATH = os.environ.get("GLMX_LIB") or os.path.join(PKG, "lib", "libglmx.so")   # GLMX_LIB: another build of it
 
 F16, F32, BF16, I32, I64 = 0, 1, 2, 3, 4
 MODE_EXACT = 1
+MODE_I16 = 2
 PHASES = 6
 OK, E_ARG, E_CUDA, E_DEVICE, E_WORKSPACE = 0, -1, -2, -3, -4
 ABI_VERSION = 1

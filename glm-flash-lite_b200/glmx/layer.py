@@ -137,10 +137,11 @@ class MoELayer:
                     pick_row=g(WS_PICK_ROW, torch.int32, ntok * topk),
                     jobs=g(WS_JOBS, torch.int32, 4 * J).reshape(J, 4))
 
-    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = _lib.MODE_EXACT,
+    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = _lib.MODE_I16,
                 out: torch.Tensor | None = None, out_dtype=torch.float32, accumulate: bool = False,
                 stream=None, events=None) -> torch.Tensor:
         """out [ntok, H] = sum over each token's picks of w * expert(x) (+ shared expert).
+        mode: 2 I16 (default; bit-identical to the reference's I16 kernel), 1 EXACT (fp16 weights, fp32 accumulation).
         events: optional list of _lib.PHASES torch.cuda.Event recorded between the kernels on the launching stream."""
         x = x.contiguous(); sel = sel.contiguous(); w = w.contiguous()
         ntok = x.shape[0]

@@ -13,6 +13,14 @@ for p in (REPO, PKG):
 
 # Parity bar of the path: layer outputs within max-abs 2e-3 x RMS(output).
 TOL_MAXABS_REL_RMS = 2e-3
+# EXACT mode (fp16 weights, fp32 accumulation, exllamav3 exact-mode semantics): the reference's own fp32 EXACT kernel
+# (moe_forward mode 1) is itself 2.5-3.1e-3 x RMS (max-abs) from its fp64 ref_expert at H=6144, because the fp16
+# rounding points turn accumulation-order differences into 1-ulp flips. The EXACT-mode check is therefore relative to
+# that kernel on the same inputs: the GPU may be at most EXACT_SLACK times as far from the fp64 truth (max-abs and
+# rel-RMS) as the reference's fp32 kernel, and never worse than the north-star bar would be for a bit-exact path.
+EXACT_SLACK = 1.25
+# K != 3 has no reference kernel (the reference is K=3 only): bound by the K=3 noise floor measured above.
+EXACT_FLOOR_MAXABS, EXACT_FLOOR_RELRMS = 4e-3, 1e-3
 
 
 def pytest_configure(config):
@@ -46,6 +54,27 @@ def parity(a, ref):
     rms = float(np.sqrt(np.mean(ref * ref))) or 1e-30
     d = a - ref
     return float(np.max(np.abs(d))) / rms, float(np.sqrt(np.mean(d * d))) / rms
+
+
+def reference_or_none():
+    """The reference's own ft_core.h (oracle/_ref), built where the reference tree was present; None if absent."""
+    try:
+        from oracle.oracle import Reference
+        return Reference()
+    except Exception:
+        return None
+
+
+def assert_exact_mode(gpu, oracle_fp64, ref_fp32=None, label=""):
+    """EXACT-mode parity: no farther from the fp64 oracle than the reference's own fp32 EXACT kernel (x EXACT_SLACK)."""
+    g_mx, g_rr = parity(gpu, oracle_fp64)
+    if ref_fp32 is not None:
+        r_mx, r_rr = parity(ref_fp32, oracle_fp64)
+        bar_mx, bar_rr = max(TOL_MAXABS_REL_RMS, EXACT_SLACK * r_mx), max(5e-4, EXACT_SLACK * r_rr)
+    else:
+        r_mx = r_rr = None
+        bar_mx, bar_rr = EXACT_FLOOR_MAXABS, EXACT_FLOOR_RELRMS
+    assert g_mx <= bar_mx and g_rr <= bar_rr, dict(label=label, gpu=(g_mx, g_rr), ref=(r_mx, r_rr), bar=(bar_mx, bar_rr))
 
 
 def cuda_ok():
