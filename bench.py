@@ -370,7 +370,8 @@ def main():
         "phase_share": dict(zip(["route", "prep", "gemv_gateup", "gemv_down", "combine"], phase_share)),
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 5 * args.steps,
+        # per step: split, input transform, gate/up GEMV, (I16: gate/up epilogue), down GEMV, combine
+        "gpu_launches": (6 if args.mode == 2 else 5) * args.steps,
         "clocks": clocks,
         "sweep": sweep,
     }

@@ -44,6 +44,8 @@ class MoELayer:
         self.has_shared = bool(has_shared)
         self.bits = tuple(int(b) for b in bits)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.device.index is None:                    # "cuda" means the current device, as in torch
+            self.device = torch.device("cuda", torch.cuda.current_device())
         et = self.E + (1 if self.has_shared else 0)
         ptrs = torch.as_tensor(trellis_ptrs, dtype=torch.int64).reshape(-1)
         if ptrs.numel() != et * 3:
