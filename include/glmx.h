@@ -112,6 +112,27 @@ GLMX_API int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint1
  * sticky ctrl words and stats (kernels/cpu_avx2/ft_tier_cu.cu:33-52, 176-193). */
 GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* workspace, void* stream, int* flags);
 
+/* Size of the scratch built into the library for glmx_moe_forward_noalloc: 48 MiB, which holds the workspace of up
+ * to 8 tokens x top-8 (+ a shared expert) at H = 6144, I = 1536, in either mode. */
+#define GLMX_NOALLOC_SCRATCH_BYTES (48u << 20)
+
+/* glmx_moe_forward without a workspace argument, for callers that cannot allocate device memory for one: a host in
+ * another language with no device allocator of its own (cgo, JNI, N-API), or a serving loop whose HBM is already
+ * held in full by its own allocator, where a cudaMalloc would fail and would also synchronise the device mid-step.
+ * No counterpart in the reference (its CPU tier owns its buffers); same arguments, work and results as
+ * glmx_moe_forward, minus the workspace.
+ *   - Scratch is a fixed device array inside the library (GLMX_NOALLOC_SCRATCH_BYTES per device); nothing is
+ *     allocated. A call whose workspace (glmx_workspace_bytes) would exceed it returns GLMX_E_WORKSPACE and runs
+ *     nothing.
+ *   - The first call on each device resolves that array's device address (one-time set-up per device, which may
+ *     load the library's device code); make that first call before any stream capture.
+ *   - All calls on one device share the one scratch: calls that overlap in time (different streams, or host threads
+ *     whose work is in flight together) race and corrupt each other's results. Calls queued on one stream are safe.
+ *   - Device-side error flags of these calls stay in the library's scratch (no workspace to hand to glmx_check). */
+GLMX_API int glmx_moe_forward_noalloc(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
+                     int sel_dtype, const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif
