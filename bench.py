@@ -29,6 +29,10 @@ H, I, E, TOPK = 6144, 1536, 288, 8
 EXPERT_BYTES_K3 = 3 * (H // 16) * (I // 16) * 96          # 10,616,832 trellis bytes per expert
 SCALE_BYTES = 3 * (H + I) * 2                              # suh + svh fp16 of gate, up, down: 46,080
 ROUTE_POOL = 16
+# DRAM bytes (read + write) per touched expert of one gate+up GEMV launch, from ncu captures of a smaller case
+# (B=16, 64 experts; traffic grows with the touched experts): I16 (profiles/gemv_i16_decode_b16.md) and EXACT
+# (profiles/gemv_gateup_exact_decode_b16.md). roofline.traffic = this x the touched experts of a full launch.
+GU_TRAFFIC_PER_EXPERT = {2: (438.0e6 + 10.0e6) / 58, 1: (414.9e6 + 4.0e6) / 57.5}
 
 
 def peaks():
@@ -39,36 +43,49 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while the block runs (warm-up + timed region):
+    one streaming nvidia-smi process, started and confirmed live before the block begins."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
         self.rows = []
-        self.stop_ev = threading.Event()
-        self.th = threading.Thread(target=self.run, daemon=True)
+        self.proc = None
+        self.th = None
+        self.first = threading.Event()
 
-    def run(self):
-        while not self.stop_ev.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"],
-                                     capture_output=True, text=True, timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([c.strip() for c in out.split(",")])
-            except Exception:
-                pass
-            self.stop_ev.wait(0.2)
+    def _read(self):
+        for line in self.proc.stdout:
+            line = line.strip()
+            if line:
+                self.rows.append([c.strip() for c in line.split(",")])
+                self.first.set()
 
     def __enter__(self):
-        self.th.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+            self.first.wait(5.0)
+        except Exception:
+            self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.stop_ev.set()
-        self.th.join(timeout=10)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.th.join(timeout=5)
 
     def summary(self):
+        if len(self.rows) > 1:
+            self.rows = self.rows[1:]          # the first sample was taken before the block put load on the GPU
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -168,7 +185,7 @@ def main():
     global E
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -365,7 +382,9 @@ def main():
                    "unique_experts_per_step": statistics.mean(r["uniq"])},
         "hbm_gbs_layer": achieved_layer_gbs,
         "roofline": {"bound": "hbm", "kernel": "gemv<gate+up>", "achieved": gu_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": gu_gbs / peak, "peak_kind": pk_kind, "traffic": None,
+                     "frac": gu_gbs / peak, "peak_kind": pk_kind,
+                     "traffic": GU_TRAFFIC_PER_EXPERT[args.mode] * statistics.mean(u + 1 for u in r["uniq"]),
+                     "traffic_unit": "bytes per launch (ncu, scaled from B=16)",
                      "layer_achieved": achieved_layer_gbs, "layer_frac": achieved_layer_gbs / peak},
         "phase_share": dict(zip(["route", "prep", "gemv_gateup", "gemv_down", "combine"], phase_share)),
         "cpu_baseline": cpu,
