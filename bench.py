@@ -6,8 +6,9 @@ A step = one glmx_moe_forward (split -> gate/up dequant-GEMV -> down dequant-GEM
 Prints ONE JSON line (rank 0). `--impl reference` times the reference's own CPU implementation (kernels/cpu_avx2
 ft_core.h, built into oracle/_ref/libftref.so) on the host cores instead.
 
-Multi-GPU (torchrun, one rank per GPU): every rank holds its own layer and runs B tokens per step (replicas of the
-single-GPU workload, weak scaling); time = max over ranks of the device time.
+Multi-GPU (torchrun, one rank per GPU): expert parallelism (configs[3]'s sharding) on the same layer and global batch:
+288/N routed experts per GPU, B/N tokens per GPU, all-gather dispatch + reduce-scatter return over NCCL (strong
+scaling: the work per step is the N=1 workload); time = max over ranks of the device time.
 """
 from __future__ import annotations
 
@@ -171,7 +172,7 @@ def run_reference_impl(args, rank, world):
     print(json.dumps({
         "impl": "reference", "metric": "moe_layer_decode_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32-acc/fp16-weights", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32-acc/fp16-weights", "data": "synthetic",
         "config": {"workload": f"configs[1] decode MoE layer B={args.batch}", "H": H, "I": I, "experts": E, "shared": 1,
                    "bits": 3, "topk": TOPK, "batch": args.batch, "mode": "EXACT"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
@@ -181,6 +182,125 @@ def run_reference_impl(args, rank, world):
 
 
 # ------------------------------------------------------------------------------------------------------------------
+def run_expert_parallel(args, rank, world, dev, dist):
+    """N > 1: configs[3]'s sharding on one layer. The 288 routed experts are split contiguously over the ranks
+    (288/N each), the shared expert is replicated; the global decode batch (args.batch, 64) is split over the ranks
+    (64/N tokens each, the tokens a data-parallel attention stage would own). A step = one expert-parallel layer
+    call (all-gather dispatch, local shard over all tokens, reduce-scatter return, shared expert overlapped).
+    Strong scaling: the total work per step is the N=1 workload. Device time, max over ranks."""
+    import torch
+    from glmx import MoELayer, ep
+
+    Bg = args.batch
+    if Bg % world or E % world:
+        raise SystemExit(f"batch {Bg} and experts {E} must divide by {world}")
+    b = Bg // world
+    first, n = ep.shard_range(E, world, rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    proj = (H // 16) * (I // 16) * 96
+
+    def bank_of(count):
+        tr = torch.randint(0, 256, (count * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
+        ptrs = torch.tensor([[tr.data_ptr() + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(count)],
+                            dtype=torch.int64)
+        sign = lambda shape: torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
+        suh = [sign((count, k)).half() for k in (H, H, I)]
+        svh = [(sign((count, m)) * (0.02 + 0.005 * torch.randn((count, m), device=dev, generator=g)).abs()).half()
+               for m in (I, I, H)]
+        return tr, ptrs, suh, svh
+
+    tr, ptrs, suh, svh = bank_of(n)
+    local = MoELayer(H, I, n, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev, first_expert=first)
+    tr_s, ptrs_s, suh_s, svh_s = bank_of(1)
+    shared = MoELayer(H, I, 1, ptrs_s, suh_s, svh_s, has_shared=False, keep=[tr_s], device=dev)
+    layer = ep.ExpertParallelLayer(local, shared, E=E)
+    stream = torch.cuda.current_stream(dev)
+    pk, pk_kind = peaks()
+
+    routes = make_routes(Bg, 1000)                         # the global routing, the same on every rank
+    sel = [torch.from_numpy(np.ascontiguousarray(s[rank * b:(rank + 1) * b])).to(dev) for s, _ in routes]
+    wts = [torch.from_numpy(np.ascontiguousarray(w[rank * b:(rank + 1) * b])).to(dev) for _, w in routes]
+    x = torch.randn((b, H), device=dev, generator=g).half()
+    out = torch.empty((b, H), dtype=torch.float32, device=dev)
+    # this shard's touched experts per step (+ the shared expert): its algorithmic bytes
+    touched = [int(np.unique(s[(s >= first) & (s < first + n)]).size) + 1 for s, _ in routes]
+
+    def timed(step_fn, steps, warmup):
+        for i in range(warmup):
+            step_fn(i)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            step_fn(i)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        t = torch.tensor([t0.elapsed_time(t1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def dev_step(i):
+        layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], mode=args.mode, out=out)
+
+    clk_idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(rank)).split(",")[int(os.environ.get("LOCAL_RANK", "0"))]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else int(os.environ.get("LOCAL_RANK", "0"))
+    with ClockSampler(clk_idx) as cs:
+        T_ms = timed(dev_step, args.steps, args.warmup)
+    clocks = cs.summary()
+    value = Bg * args.steps / (T_ms / 1e3)
+    my_bytes = sum(touched[i % ROUTE_POOL] for i in range(args.steps)) * (EXPERT_BYTES_K3 + SCALE_BYTES)
+    tb = torch.tensor([float(my_bytes)], device=dev, dtype=torch.float64)
+    dist.all_reduce(tb)
+    layer_gbs = float(tb.item()) / (T_ms / 1e3) / 1e9
+
+    # end to end: this rank's tokens from pinned host memory, result back to pinned host memory
+    x_h = torch.randn((b, H)).half().pin_memory()
+    sel_h = [s.cpu().pin_memory() for s in sel]
+    w_h = [w.cpu().pin_memory() for w in wts]
+    out_h = torch.empty((b, H), dtype=torch.float32).pin_memory()
+    x_d = torch.empty_like(x); s_d = torch.empty_like(sel[0]); w_d = torch.empty_like(wts[0])
+
+    def e2e_step(i):
+        x_d.copy_(x_h, non_blocking=True); s_d.copy_(sel_h[i % ROUTE_POOL], non_blocking=True)
+        w_d.copy_(w_h[i % ROUTE_POOL], non_blocking=True)
+        layer.forward(x_d, s_d, w_d, mode=args.mode, out=out)
+        out_h.copy_(out, non_blocking=True)
+
+    E_ms = timed(e2e_step, args.steps, args.warmup)
+    dist.barrier()
+    del layer
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak = pk["hbm_gbs"] * world
+    line = {
+        "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
+        "config": {"workload": f"configs[3] sharding on one configs[1] layer: B={Bg} global decode tokens, {E} routed "
+                               f"experts split {n}/GPU + replicated shared expert, H=6144, I=1536, K=3, top-8",
+                   "batch": Bg, "tokens_per_gpu": b, "experts_per_gpu": n, "H": H, "I": I, "bits": 3, "topk": TOPK,
+                   "mode": {1: "EXACT", 2: "I16"}[args.mode], "parallelism": f"ep{world}",
+                   "l2": "inputs larger than L2 (touched trellis per step > 126 MB)"},
+        "hbm_gbs_layer": layer_gbs,
+        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer step (all ranks)", "achieved": layer_gbs,
+                     "peak": peak, "unit": "GB/s", "frac": layer_gbs / peak, "peak_kind": pk_kind + f" x {world}",
+                     "traffic": None},
+        "cpu_baseline": None,
+        "e2e": {"value": Bg * args.steps / (E_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": world * (b * H * 2 + b * TOPK * 8),
+                "d2h_bytes_per_step": world * b * H * 4},
+        # per step and rank: split + transform + gate/up + epilogue + down + combine, for the shard and the shared expert
+        "gpu_launches": (12 if args.mode == 2 else 10) * args.steps * world,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     global E
     ap = argparse.ArgumentParser()
@@ -221,6 +341,9 @@ def main():
 
     from glmx import MoELayer
     from glmx import _lib
+
+    if world > 1:
+        return run_expert_parallel(args, rank, world, dev, dist)
 
     # ---- synthetic layer on the device: 289 experts x (gate|up|down) K=3 trellis + scales ----
     g = torch.Generator(device=dev)
@@ -374,7 +497,7 @@ def main():
     line = {
         "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
         "config": {"workload": f"configs[1] decode MoE layer B={B} (288 routed + 1 shared, H=6144, I=1536, K=3, top-8)",
                    "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": {1: "EXACT", 2: "I16"}[args.mode],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",

@@ -71,6 +71,7 @@ int glmx_layer_create(const glmx_layer_desc* d, glmx_layer** out)
         L.svh[p] = static_cast<const uint16_t*>(d->svh[p]);
     }
     L.act_limit = d->act_limit;
+    L.first = d->first_expert;
     cudaError_t e = cudaGetDevice(&L.device);
     if (e != cudaSuccess) { delete l; return cuda_fail(e, "glmx_layer_create: cudaGetDevice"); }
     if (L.device >= 64) { delete l; return fail(GLMX_E_ARG, "glmx_layer_create: device index >= 64"); }

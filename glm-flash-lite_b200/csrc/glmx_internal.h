@@ -17,6 +17,7 @@ struct Layer
     int H = 0, I = 0, E = 0, E_total = 0, has_shared = 0;
     int bits[3] = { 3, 3, 3 };
     float act_limit = 0.0f;
+    int first = 0;                     // global id of routed expert 0 (expert-parallel shards)
     int device = 0;
     uint64_t* d_trellis = nullptr;     // device [E_total][3] addresses (gate, up, down)
     const uint16_t* suh[3] = {};       // device fp16 [E_total][k]

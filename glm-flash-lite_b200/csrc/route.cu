@@ -28,6 +28,7 @@ struct RouteArgs
     const void* sel; int sel_i64;
     const void* w; int w_dtype;
     int ntok, topk, E, has_shared;
+    int first;                // global id of local expert 0
     int maxm;                 // rows per job (8 EXACT, 4 I16)
     int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
     int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
@@ -37,10 +38,13 @@ struct RouteArgs
     int* cnt_gu; int* cnt_d; int* err;
 };
 
+// local expert id of pick p: sel - first; anything outside [0, E) (masked picks, other shards' experts) is skipped
 __device__ __forceinline__ int load_sel(const RouteArgs& a, int p)
 {
-    return a.sel_i64 ? (int) max((long long) -1, min((long long) 0x7fffffff, reinterpret_cast<const long long*>(a.sel)[p]))
-                     : reinterpret_cast<const int*>(a.sel)[p];
+    const long long g = a.sel_i64 ? reinterpret_cast<const long long*>(a.sel)[p] : (long long) reinterpret_cast<const int*>(a.sel)[p];
+    if (g < 0) return -1;
+    const long long e = g - a.first;
+    return (e >= 0 && e < a.E) ? (int) e : -1;
 }
 
 __device__ __forceinline__ float load_w(const RouteArgs& a, int p)
@@ -210,7 +214,7 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
     RouteArgs a;
     a.maxm = maxm;
     a.sel = sel; a.sel_i64 = sel_i64; a.w = w; a.w_dtype = w_dtype;
-    a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared;
+    a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared; a.first = L.first;
     a.nb_gu = L.I / 128; a.nb_d = L.H / 128; a.kq_gu = L.H / 128; a.kq_d = L.I / 128;
     a.grid_ctas = grid_ctas;
     a.part_slots = lay.part_slots;

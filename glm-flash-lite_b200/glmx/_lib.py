@@ -14,7 +14,7 @@ MODE_EXACT = 1
 MODE_I16 = 2
 PHASES = 6
 OK, E_ARG, E_CUDA, E_DEVICE, E_WORKSPACE = 0, -1, -2, -3, -4
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _P = C.c_void_p
 _I = C.c_int
@@ -23,7 +23,8 @@ _I = C.c_int
 class LayerDesc(C.Structure):
     """glmx_layer_desc of include/glmx.h"""
     _fields_ = [("hidden", _I), ("intermediate", _I), ("n_experts", _I), ("has_shared", _I),
-                ("bits", _I * 3), ("trellis", _P), ("suh", _P * 3), ("svh", _P * 3), ("act_limit", C.c_float)]
+                ("bits", _I * 3), ("trellis", _P), ("suh", _P * 3), ("svh", _P * 3), ("act_limit", C.c_float),
+                ("first_expert", _I)]
 
 
 class GlmxError(RuntimeError):

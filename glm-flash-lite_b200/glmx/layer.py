@@ -32,13 +32,14 @@ class MoELayer:
     """One MoE layer of E routed experts (+ optional shared expert) resident in HBM.
 
     trellis_ptrs: int64 [E_total, 3] device addresses of the native-layout gate / up / down trellis tensors (the pointer
-    table exllamav3 keeps per expert, glm53/expert_cache.py:603-616, and tier_add_layer's `ptrs`, ft_tier_ext.cpp:159).
+    table exllamav3 keeps per expert, glm53/expert_cache.py:603-616, and tier_add_layer's `ptrs`, ft_tier_ext.cpp:160).
     suh / svh: three fp16 CUDA tensors each, [E_total, k] and [E_total, n] (tier_add_layer's scale shapes).
     keep: tensors that own the memory behind trellis_ptrs (kept alive by the layer).
+    first_expert: global id of routed expert 0 (an expert-parallel shard); picks outside the shard are skipped.
     """
 
     def __init__(self, H: int, I: int, E: int, trellis_ptrs, suh, svh, bits=(3, 3, 3), has_shared: bool = False,
-                 act_limit: float = 0.0, keep=(), device=None):
+                 act_limit: float = 0.0, keep=(), device=None, first_expert: int = 0):
         self.lib = _lib.load()
         self.H, self.I, self.E = int(H), int(I), int(E)
         self.has_shared = bool(has_shared)
@@ -62,6 +63,8 @@ class MoELayer:
             d.svh[p] = self.svh[p].data_ptr()
         d.trellis = self._ptrs.ctypes.data
         d.act_limit = float(act_limit)
+        d.first_expert = int(first_expert)
+        self.first_expert = int(first_expert)
         h = C.c_void_p()
         with torch.cuda.device(self.device):
             check(self.lib.glmx_layer_create(C.byref(d), C.byref(h)))

@@ -50,7 +50,7 @@ def matrix_bytes(k: int, n: int, bits: int) -> int:
 class ExpertBank:
     """Host copy of E experts (+ optional shared expert, stored as the last expert) in the packed bank layout:
     per expert gate | up | down trellis bytes, experts contiguous. Scales follow tier_add_layer's shapes
-    (ft_tier_ext.cpp:159-183): suh/svh fp16 [E, k] / [E, n] per projection."""
+    (ft_tier_ext.cpp:160-183): suh/svh fp16 [E, k] / [E, n] per projection."""
     H: int
     I: int
     E: int                      # routed experts

@@ -17,7 +17,7 @@
 extern "C" {
 #endif
 
-#define GLMX_ABI_VERSION 1
+#define GLMX_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define GLMX_API __attribute__((visibility("default")))
@@ -47,7 +47,7 @@ typedef struct glmx_layer glmx_layer;
 
 /* One MoE layer's routed experts (+ optional shared expert as the last entry), HBM-resident, native EXL3 layout:
  * tile (tk, tn) of a [k x n] projection at byte (tk * (n/16) + tn) * 32 * bits. Replaces the registration of
- * tier_add_layer(li, ptrs int64 [E,3], suh_g, svh_g, suh_u, svh_u, suh_d, svh_d) (kernels/cpu_avx2/ft_tier_ext.cpp:159-183)
+ * tier_add_layer(li, ptrs int64 [E,3], suh_g, svh_g, suh_u, svh_u, suh_d, svh_d) (kernels/cpu_avx2/ft_tier_ext.cpp:160-183)
  * and the per-expert pointer tables exllamav3 keeps (ptrs_trellis, glm53/expert_cache.py:603-616). */
 typedef struct
 {
@@ -60,6 +60,10 @@ typedef struct
     const void* suh[3];               /* device fp16 [(E + has_shared), k] input sign/scale vectors per projection */
     const void* svh[3];               /* device fp16 [(E + has_shared), n] output scale vectors per projection */
     float act_limit;                  /* SwiGLU clamp (0 = off), tier_set_act_limit (ft_tier_ext.cpp:635) */
+    int first_expert;                 /* global id of routed expert 0 of this layer (an expert-parallel shard holds
+                                         ids [first_expert, first_expert + n_experts)); picks are read as
+                                         sel - first_expert. ft_split's `first` / the module's `routing_first`
+                                         (kernels/cpu_avx2/ft_tier_cu.cu:22, glm53/cpu_tier.py:293-299) */
 } glmx_layer_desc;
 
 GLMX_API int glmx_version(void);
@@ -76,7 +80,8 @@ GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk
 /* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
  * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward in I16 mode uses jobs of <= 4 rows). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
  * kernels/k110/ft_split_fast.cu:200-235) and the job grouping of moe_forward (kernels/cpu_avx2/ft_core.h:1344-1349).
- * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64); ids outside [0, E) are skipped.
+ * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64) of global expert ids; ids outside
+ * [first_expert, first_expert + E) are skipped (negative ids mask a pick).
  * w: device [ntok, topk] fp32 / fp16 / bf16. */
 GLMX_API int glmx_route(const glmx_layer* layer, const void* sel, int sel_dtype, const void* w, int w_dtype, int ntok, int topk,
                void* workspace, size_t workspace_bytes, void* stream);
@@ -89,7 +94,7 @@ GLMX_API int glmx_workspace_array(const glmx_layer* layer, int ntok, int topk, i
 /* Whole routed-MoE layer on the GPU: split -> gate/up dequant-GEMV + SiLU*up -> down dequant-GEMV -> weighted
  * combine (+ shared expert, weight 1). out [ntok, H] (fp32 or fp16) = sum over token picks of w * expert(x) + shared(x);
  * accumulate = 1 adds into out instead (ft_combine's `out += partial`, kernels/cpu_avx2/ft_tier_cu.cu:226-233).
- * Replaces tier_forward(li, x fp32 [m,H], sel int32 [m,k], w fp32 [m,k], mode) (kernels/cpu_avx2/ft_tier_ext.cpp:864-904)
+ * Replaces tier_forward(li, x fp32 [m,H], sel int32 [m,k], w fp32 [m,k], mode) (kernels/cpu_avx2/ft_tier_ext.cpp:865-904)
  * and the GPU expert path it stands beside (exllamav3 BlockSparseMLP experts). x: device [ntok, H] fp16 / fp32 / bf16. */
 GLMX_API int glmx_moe_forward(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
                      const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,

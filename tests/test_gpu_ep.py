@@ -1,0 +1,80 @@
+"""Expert parallelism on 2 GPUs (NCCL): each rank's output against the single-GPU layer over the same global batch.
+Skipped on a box with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+H, I, E, K, B = 1024, 512, 16, 4, 6
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(rank):
+    from glmx import synth
+    x = synth.make_x(B, H, 500 + rank)
+    sel, w = synth.route_uniform(B, E, K, 600 + rank)
+    if rank == 0:
+        sel[1, 2] = -1
+    return x, sel, w
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "glm-flash-lite_b200"))
+    import torch.distributed as dist
+    from glmx import MoELayer, ep, synth
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        bank = synth.make_bank(H, I, E, shared=True, seed=77)
+        layer = ep.from_bank(bank, device=dev)
+        full = MoELayer.from_bank(bank, device=dev)
+        xs = [_inputs(r) for r in range(world)]
+        xg = np.concatenate([a for a, _, _ in xs]); sg = np.concatenate([s for _, s, _ in xs]); wg = np.concatenate([w for _, _, w in xs])
+        res = {}
+        for mode in (2, 1):
+            x, s, w = (torch.from_numpy(a).to(dev) for a in xs[rank])
+            got = layer.forward(x, s, w, mode=mode)
+            got2 = layer.forward(x, s, w, mode=mode)          # a second call reuses the buffers
+            want = full.forward(torch.from_numpy(xg).to(dev), torch.from_numpy(sg).to(dev), torch.from_numpy(wg).to(dev),
+                                mode=mode)[rank * B:(rank + 1) * B]
+            g, g2, wnt = got.cpu().numpy().astype(np.float64), got2.cpu().numpy(), want.cpu().numpy().astype(np.float64)
+            rms = float(np.sqrt(np.mean(wnt * wnt)))
+            res[mode] = (float(np.max(np.abs(g - wnt))) / rms, bool(np.array_equal(got.cpu().numpy(), g2)))
+        q.put((rank, res))
+    except Exception as ex:  # report to the parent instead of hanging it
+        q.put((rank, repr(ex)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_match_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert isinstance(v, dict), (r, v)
+        # I16: per-expert results are bit-identical; only the order of the cross-shard sum differs
+        assert v[2][0] <= 1e-5 and v[2][1], (r, v)
+        # EXACT: the shard's split-K schedule differs from the full layer's, so fp16 rounding points may flip
+        assert v[1][0] <= 2e-3 and v[1][1], (r, v)
