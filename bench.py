@@ -182,6 +182,137 @@ def run_reference_impl(args, rank, world):
 
 
 # ------------------------------------------------------------------------------------------------------------------
+def run_prefill(args, dev):
+    """one layer (288 routed + 1 shared) at prefill, T tokens (4096) of bf16 activations ~ N(0,1), expert
+    popularity Zipf(1.1) over a seeded permutation, top-8. EXACT mode through the tensor-core GEMM path. Metric:
+    TFLOP/s of useful work = 2 * 3 * H * I * T * (8 + 1) per call / device time."""
+    import torch
+    from glmx import MoELayer, _lib, synth
+
+    T = args.tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    et = E + 1
+    bank = torch.randint(0, 256, (et * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
+    proj = (H // 16) * (I // 16) * 96
+    ptrs = torch.tensor([[bank.data_ptr() + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(et)],
+                        dtype=torch.int64)
+    sign = lambda shape: torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
+    suh = [sign((et, k)).half() for k in (H, H, I)]
+    svh = [(sign((et, n)) * (0.02 + 0.005 * torch.randn((et, n), device=dev, generator=g)).abs()).half() for n in (I, I, H)]
+    layer = MoELayer(H, I, E, ptrs, suh, svh, bits=(3, 3, 3), has_shared=True, keep=[bank], device=dev)
+    stream = torch.cuda.current_stream(dev)
+    pk, pk_kind = peaks()
+    npool = 4
+    routes = [synth.route_zipf(T, E, TOPK, 1.1, 2000 + i) for i in range(npool)]
+    sel = [torch.from_numpy(s).to(dev) for s, _ in routes]
+    wts = [torch.from_numpy(w).to(dev) for _, w in routes]
+    x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty((T, H), dtype=torch.float32, device=dev)
+    mode = _lib.MODE_EXACT | _lib.PATH_GEMM
+    flop = 2.0 * 3 * H * I * T * (TOPK + 1)
+    steps = args.steps
+    ph = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.PHASES)] for _ in range(steps)]
+    for i in range(args.warmup):
+        layer.forward(x, sel[i % npool], wts[i % npool], out=out, mode=mode)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+    clk_idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]) if os.environ.get("CUDA_VISIBLE_DEVICES") else 0
+    with ClockSampler(clk_idx) as cs:
+        t0.record(stream)
+        for i in range(steps):
+            layer.forward(x, sel[i % npool], wts[i % npool], out=out, mode=mode, events=ph[i])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    clocks = cs.summary()
+    flags = layer.check_device(T, TOPK)
+    if flags:
+        raise RuntimeError(f"device error flags {flags}")
+    T_ms = t0.elapsed_time(t1)
+    step_ms = [ph[i][0].elapsed_time(ph[i][5]) for i in range(steps)]
+    phase_ms = [[ph[i][k].elapsed_time(ph[i][k + 1]) for k in range(_lib.PHASES - 1)] for i in range(steps)]
+    tflops = flop * steps / (T_ms / 1e3) / 1e12
+    gu_ms = sum(p[2] for p in phase_ms)
+    d_ms = sum(p[3] for p in phase_ms)
+    gu_tflops = (2.0 * 2 * H * I * T * (TOPK + 1)) * steps / (gu_ms / 1e3) / 1e12
+    d_tflops = (2.0 * H * I * T * (TOPK + 1)) * steps / (d_ms / 1e3) / 1e12
+    phase_share = [sum(p[k] for p in phase_ms) / sum(step_ms) for k in range(_lib.PHASES - 1)]
+    # rows per expert of the routings (tile efficiency of the 128-row jobs)
+    counts = [np.bincount(s.reshape(-1), minlength=E) for s, _ in routes]
+    rows_real = np.mean([c.sum() + T for c in counts])
+    rows_tiles = np.mean([(np.ceil(c / 128).sum() + np.ceil(T / 128)) * 128 for c in counts])
+
+    # e2e: bf16 activations and routing from pinned host memory, fp32 result back
+    x_h = x.cpu().pin_memory(); s_h = [s.cpu().pin_memory() for s in sel]; w_h = [w.cpu().pin_memory() for w in wts]
+    out_h = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    x_d = torch.empty_like(x); s_d = torch.empty_like(sel[0]); w_d = torch.empty_like(wts[0])
+    def e2e_step(i):
+        x_d.copy_(x_h, non_blocking=True); s_d.copy_(s_h[i % npool], non_blocking=True); w_d.copy_(w_h[i % npool], non_blocking=True)
+        layer.forward(x_d, s_d, w_d, out=out, mode=mode)
+        out_h.copy_(out, non_blocking=True)
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            from oracle import oracle as O
+            if os.path.exists(O.REF_SO):
+                thr = cpu_threads()
+                ref = O.Reference()
+                hb = synth.make_bank(H, I, E, shared=True, seed=0)
+                rl = ref.layer(hb, with_shared=True)
+                cpus = sorted(os.sched_getaffinity(0))
+                ref.start_pool(thr, cpus[:thr])
+                Tc = 128
+                s0, w0 = synth.route_zipf(Tc, E, TOPK, 1.1, 2000)
+                xs = x[:Tc].float().cpu().numpy()
+                pr = O.with_shared_routes(s0, w0, E)
+                calls, t_start = 0, time.perf_counter()
+                while time.perf_counter() - t_start < args.cpu_seconds or calls < 1:
+                    ref.moe_forward(rl, xs, *pr, mode=1, band=True)
+                    calls += 1
+                dt = time.perf_counter() - t_start
+                ref.stop_pool()
+                cflop = 2.0 * 3 * H * I * Tc * (TOPK + 1) * calls
+                cpu = {"value": cflop / dt / 1e12, "unit": "TFLOP/s", "cores": thr, "kind": "reference",
+                       "sample": f"{calls} calls of the reference moe_forward_band (EXACT) on {Tc} tokens of the same "
+                                 f"Zipf(1.1) routing ({dt:.1f} s)"}
+        except Exception as ex:
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference", "sample": f"failed: {ex!r}"[:200]}
+
+    peak = pk["bf16_tflops"]
+    line = {
+        "metric": "moe_layer_prefill_tflops", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": T_ms / steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16-weights/fp16-act/fp32-acc", "data": "synthetic",
+        "config": {"workload": f"configs[2] prefill MoE layer: {T} tokens, Zipf(1.1) routing over 288 routed experts "
+                               f"+ shared, top-8, H=6144, I=1536, K=3, bf16 activations", "tokens": T, "H": H, "I": I,
+                   "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": "EXACT (tensor-core GEMM path)",
+                   "l2": "inputs larger than L2 (activations 2 x 453 MB, trellis 3.1 GB)",
+                   "rows": rows_real, "tile_rows": rows_tiles, "tile_efficiency": rows_real / rows_tiles},
+        "roofline": {"bound": "tensor", "kernel": "gemm_pf<gate+up>", "achieved": gu_tflops, "peak": peak,
+                     "unit": "TFLOP/s", "frac": gu_tflops / peak, "peak_kind": pk_kind + " bf16 burst",
+                     "frac_of_sustained": gu_tflops / pk["bf16_tflops_sustained"], "traffic": None,
+                     "down_achieved": d_tflops, "layer_achieved": tflops, "layer_frac": tflops / peak},
+        "phase_share": dict(zip(["route", "prep", "gemm_gateup+epilogue", "gemm_down", "combine"], phase_share)),
+        "cpu_baseline": cpu,
+        "e2e": {"value": flop * steps / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": T * H * 2 + T * TOPK * 8, "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": 6 * steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_expert_parallel(args, rank, world, dev, dist):
     """N > 1: configs[3]'s sharding on one layer. The 288 routed experts are split contiguously over the ranks
     (288/N each), the shared expert is replicated; the global decode batch (args.batch, 64) is split over the ranks
@@ -314,6 +445,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")
     ap.add_argument("--profile", action="store_true", help="device steps only (no e2e, sweep or CPU baseline): for ncu")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: configs[1] (the headline); prefill: configs[2] (4096 tokens, Zipf routing, TFLOP/s)")
+    ap.add_argument("--tokens", type=int, default=4096, help="prefill tokens")
     ap.add_argument("--mode", type=int, default=2, choices=[1, 2], help="1 EXACT (fp16 weights, fp32 tensor-core sums), "
                     "2 I16 (int16 activations, exact integer tensor-core sums; bit-identical to the reference's I16 mode)")
     args = ap.parse_args()
@@ -342,6 +476,10 @@ def main():
     from glmx import MoELayer
     from glmx import _lib
 
+    if args.workload == "prefill":
+        if world > 1:
+            raise SystemExit("the prefill workload runs on one GPU")
+        return run_prefill(args, dev)
     if world > 1:
         return run_expert_parallel(args, rank, world, dev, dist)
 

@@ -173,8 +173,18 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     int grid;
     int rc = check_common(l, ntok, topk, sel_dtype, w_dtype, ws, ws_bytes, &lay, &grid, "glmx_moe_forward");
     if (rc) return rc;
-    if (mode != GLMX_MODE_EXACT && mode != GLMX_MODE_I16)
-        return fail(GLMX_E_ARG, "glmx_moe_forward: mode must be GLMX_MODE_EXACT (1) or GLMX_MODE_I16 (2)");
+    const int base = mode & 0xff, path = mode & (GLMX_PATH_GEMV | GLMX_PATH_GEMM);
+    if ((base != GLMX_MODE_EXACT && base != GLMX_MODE_I16) || (mode & ~(0xff | GLMX_PATH_GEMV | GLMX_PATH_GEMM)) ||
+        path == (GLMX_PATH_GEMV | GLMX_PATH_GEMM))
+        return fail(GLMX_E_ARG, "glmx_moe_forward: mode must be GLMX_MODE_EXACT (1) or GLMX_MODE_I16 (2), optionally with one "
+                                "of GLMX_PATH_GEMV / GLMX_PATH_GEMM");
+    if (base == GLMX_MODE_I16 && path == GLMX_PATH_GEMM)
+        return fail(GLMX_E_ARG, "glmx_moe_forward: the tensor-core GEMM path is EXACT mode only");
+    if (base == GLMX_MODE_I16 && lay.rows_max > I16_MAX_ROWS)
+        return fail(GLMX_E_ARG, "glmx_moe_forward: I16 is the decode mode (at most " + std::to_string(I16_MAX_ROWS) +
+                                " rows = picks + shared-expert rows per call); use GLMX_MODE_EXACT for larger batches");
+    const bool gemm = base == GLMX_MODE_EXACT &&
+                      (path == GLMX_PATH_GEMM || (path == 0 && lay.rows_max >= PF_AUTO_ROWS_PER_EXPERT * l->L.E_total));
     if (x_dtype != GLMX_F16 && x_dtype != GLMX_F32 && x_dtype != GLMX_BF16)
         return fail(GLMX_E_ARG, "glmx_moe_forward: x dtype must be fp16, fp32 or bf16");
     if (out_dtype != GLMX_F16 && out_dtype != GLMX_F32) return fail(GLMX_E_ARG, "glmx_moe_forward: out dtype must be fp16 or fp32");
@@ -185,14 +195,16 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     cudaError_t e = cudaSuccess;
     if (events && events[0]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[0]), st);
-    const int maxm = mode == GLMX_MODE_I16 ? I16_MAXM : MAXM;
+    const int maxm = base == GLMX_MODE_I16 ? I16_MAXM : gemm ? PF_MAXM : MAXM;
     if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, maxm, wsb, lay, grid, st);
     if (e == cudaSuccess && events && events[1]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[1]), st);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: route launch");
-    if (mode == GLMX_MODE_I16)
+    if (base == GLMX_MODE_I16)
         e = launch_i16_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events);
+    else if (gemm)
+        e = launch_prefill_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events);
     else
-        e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, mode, out, out_dtype, accumulate, wsb, lay, grid, st, events);
+        e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, base, out, out_dtype, accumulate, wsb, lay, grid, st, events);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: launch");
     return GLMX_OK;
 }

@@ -62,8 +62,20 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
 cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
                                int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events);
 cudaError_t launch_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, cudaStream_t st);
+// prefill path (tensor-core GEMM, EXACT mode) and the two kernels it shares with the GEMV paths
+cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
+                                   int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events);
+// EXACT input transform of every row (xg, xu: fp16 [R][H], PERM16 order)
+cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st);
+// down out_block of raw fp32 rows [R][H] + weighted sum in pick order (+ shared expert) into out
+cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
+                               uint8_t* ws, const WsLayout& lay, cudaStream_t st);
 
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
+constexpr int I16_MAX_ROWS = 8192;     // I16 is the decode mode: its activation layout is sized for up to this many rows
+constexpr int PF_MAXM = 128;           // rows per job of the prefill GEMM (one tensor-core tile)
+constexpr int PF_AUTO_ROWS_PER_EXPERT = 32;   // EXACT mode takes the GEMM path from this many rows per expert on average
+constexpr int PF_KSPLIT = 3;           // K splits of the prefill gate/up GEMM (partial sums added in order in fp32)
 
 }  // namespace glmx

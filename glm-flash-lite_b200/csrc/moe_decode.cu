@@ -510,19 +510,39 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.xd = take(sizeof(__half) * (size_t) rows * L.I);
     w.yrow = take(sizeof(float) * (size_t) rows * L.H);
     w.partials = take(sizeof(float) * (size_t) w.part_slots * 2 * MAXM * 128 + 0 * nmax);
-    // I16 mode: jobs of <= I16_MAXM rows of one expert: at most rows/4 + one partial job per expert
-    const int ji = rows < (rows + 3) / 4 + L.E_total ? rows : (rows + 3) / 4 + L.E_total;
+    // raw fp32 gate/up outputs (I16 GEMV: one slice; prefill GEMM: one slice per K split)
+    w.yraw_gu = take(sizeof(float) * (size_t) PF_KSPLIT * rows * 2 * L.I);
+    // I16 mode (decode-sized calls only): jobs of <= I16_MAXM rows of one expert: at most rows/4 + one partial job per
+    // expert
+    const int ji = rows <= I16_MAX_ROWS ? (rows < (rows + 3) / 4 + L.E_total ? rows : (rows + 3) / 4 + L.E_total) : 0;
     w.jobs_max_i16 = ji;
     const int BH = L.H / 128, BI = L.I / 128;
     w.actb_gu = take((size_t) ji * 2 * BH * I16_ACT_BYTES);
     w.sc_gu = take(sizeof(float) * 4 * (size_t) ji * 2 * BH);
-    w.psum_gu = take(sizeof(float) * (size_t) rows * 2 * BH);
-    w.yraw_gu = take(sizeof(float) * (size_t) rows * 2 * L.I);
+    w.psum_gu = take(sizeof(float) * (size_t) (ji ? rows : 0) * 2 * BH);
     w.actb_d = take((size_t) ji * BI * I16_ACT_BYTES);
     w.sc_d = take(sizeof(float) * 4 * (size_t) ji * BI);
-    w.psum_d = take(sizeof(float) * (size_t) rows * BI);
+    w.psum_d = take(sizeof(float) * (size_t) (ji ? rows : 0) * BI);
     w.total = o;
     return w;
+}
+
+cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st)
+{
+    const int rows = lay.rows_max;
+    if (rows <= 0) return cudaSuccess;
+    PrepArgs p;
+    p.plan = reinterpret_cast<const Plan*>(ws + lay.plan); p.x = x; p.x_dtype = x_dtype; p.H = L.H;
+    p.row_token = reinterpret_cast<const int*>(ws + lay.row_token);
+    p.row_expert = reinterpret_cast<const int*>(ws + lay.row_expert);
+    p.suh_g = reinterpret_cast<const __half*>(L.suh[0]);
+    p.suh_u = reinterpret_cast<const __half*>(L.suh[1]);
+    p.xg = reinterpret_cast<__half*>(ws + lay.xg);
+    p.xu = reinterpret_cast<__half*>(ws + lay.xu);
+    p.rows_max = rows;
+    const long long warps = (long long) rows * 2 * (L.H / 128);
+    prep_kernel<<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(p);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,

@@ -445,6 +445,24 @@ cudaError_t launch_gu_i16_k0(const Layer& L, const GemvI16Args& a, cudaStream_t 
 
 }  // namespace
 
+cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
+                               uint8_t* ws, const WsLayout& lay, cudaStream_t st)
+{
+    if (ntok <= 0) return cudaSuccess;
+    CombineI16Args c;
+    c.plan = reinterpret_cast<const Plan*>(ws + lay.plan);
+    c.pick_row = reinterpret_cast<const int*>(ws + lay.pick_row);
+    c.row_weight = reinterpret_cast<const float*>(ws + lay.row_weight);
+    c.row_expert = reinterpret_cast<const int*>(ws + lay.row_expert);
+    c.yraw = yraw;
+    c.svh_d = reinterpret_cast<const __half*>(L.svh[2]);
+    c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared; c.E = L.E;
+    c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
+    const long long w3 = (long long) ntok * (L.H / 128);
+    combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
                                int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events)
 {

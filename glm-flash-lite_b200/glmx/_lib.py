@@ -12,6 +12,7 @@ LIB_PATH = os.environ.get("GLMX_LIB") or os.path.join(PKG, "lib", "libglmx.so") 
 F16, F32, BF16, I32, I64 = 0, 1, 2, 3, 4
 MODE_EXACT = 1
 MODE_I16 = 2
+PATH_GEMV, PATH_GEMM = 0x100, 0x200    # OR'ed into MODE_EXACT: force the decode GEMV or the prefill GEMM kernels
 PHASES = 6
 OK, E_ARG, E_CUDA, E_DEVICE, E_WORKSPACE = 0, -1, -2, -3, -4
 ABI_VERSION = 2

@@ -41,7 +41,14 @@ extern "C" {
 /* numeric modes, same numbering as the reference's moe_forward (kernels/cpu_avx2/ft_core.h:822-823) */
 #define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights (GPU-exact), fp32 tensor-core accumulation */
 #define GLMX_MODE_I16 2     /* int16 activations per 128-block, exact integer tensor-core sums, the reference's fp32
-                               flush order (ft_core.h:418-598): bit-identical to the reference's I16 mode */
+                               flush order (ft_core.h:418-598): bit-identical to the reference's I16 mode. The decode
+                               mode: at most 8192 rows (picks + shared-expert rows) per call */
+/* Path selection, OR'ed into the mode (EXACT only; default: chosen from the batch): GEMV = the decode kernels (one pass
+ * over each expert's trellis per job of <= 8 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
+ * <= 128 rows, trellis decoded into shared memory once per 128-row tile), the default once the call has >= 32 rows per
+ * expert on average. The reference's large-batch schedule is moe_forward_band (ft_core.h:1617-1651). */
+#define GLMX_PATH_GEMV 0x100
+#define GLMX_PATH_GEMM 0x200
 
 typedef struct glmx_layer glmx_layer;
 
