@@ -169,6 +169,17 @@ __device__ __forceinline__ void decode_words(const uint8_t* tile, const LaneDeco
     for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
 }
 
+// decode_words from the lane's two stream words already loaded (hi = word at off_hi, lo = word at off_lo), so a
+// caller can issue the shared-memory loads of several tiles before any of their arithmetic
+template <int K>
+__device__ __forceinline__ void decode_words_from(uint32_t hi, uint32_t lo, const LaneDecode<K>& L, uint32_t x[8])
+{
+    const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
+    const uint32_t hi2 = hi >> L.pre;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
+}
+
 // mma.m16n8k32, A = product bytes (u8), B = activation planes (s8), exact int32 accumulation
 __device__ __forceinline__ void imma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
 {
@@ -183,6 +194,22 @@ __device__ __forceinline__ void decode_frag_tc(const uint8_t* tile, const LaneDe
 {
     uint32_t x[8];
     decode_words<K>(tile, L, x);
+    uint32_t d1[4], d2[4];
+    imma_bytesum(d1, x[0], x[4], x[1], x[5], ones.b0, ones.b1, 0x6400u);
+    imma_bytesum(d2, x[2], x[6], x[3], x[7], ones.b0, ones.b1, 0x6400u);
+    a[0] = codebook_pair(d1[0], d1[1]);
+    a[1] = codebook_pair(d1[2], d1[3]);
+    a[2] = codebook_pair(d2[0], d2[1]);
+    a[3] = codebook_pair(d2[2], d2[3]);
+}
+
+// decode_frag_tc from preloaded stream words (see decode_words_from)
+template <int K>
+__device__ __forceinline__ void decode_frag_tc_from(uint32_t hi, uint32_t lo, const LaneDecode<K>& L, const OnesFrag& ones,
+                                                    uint32_t a[4])
+{
+    uint32_t x[8];
+    decode_words_from<K>(hi, lo, L, x);
     uint32_t d1[4], d2[4];
     imma_bytesum(d1, x[0], x[4], x[1], x[5], ones.b0, ones.b1, 0x6400u);
     imma_bytesum(d2, x[2], x[6], x[3], x[7], ones.b0, ones.b1, 0x6400u);

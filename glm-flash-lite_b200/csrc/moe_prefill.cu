@@ -1,19 +1,20 @@
 // Routed-expert MoE layer for prefill-sized batches (many rows per expert), EXACT mode: a grouped GEMM on the
-// 5th-generation tensor cores. Per (job of <= 128 rows of one expert, 128-column block, projection, K split) tile:
+// 5th-generation tensor cores. Per (job of <= 128 rows of one expert, column block of TN = 256 (else 128) outputs,
+// projection, K split) tile:
 //
 //   A  = the rows' transformed activations (fp16, PERM16 order inside each 16-input group), [128 x 64] per stage,
 //        loaded by the tensor-memory-access unit from the row-major activation buffer with the 128-byte swizzle
-//   B  = the expert's trellis tiles for the stage (4 k-rows x 8 tiles), bulk-copied to shared memory, decoded by 8
-//        warps into fp16 (tensor-core byte sums + codebook FMA, decode_frag_tc) and written with stmatrix into the
-//        K-major interleaved layout the MMA reads
-//   D  = fp32 accumulators in tensor memory (tcgen05.mma kind::f16, M=128, N=128, K=16 per instruction). Long K sums
+//   B  = the expert's trellis tiles for the stage (4 k-rows x TN/16 tiles), bulk-copied to shared memory, decoded by
+//        8 warps into fp16 (tensor-core byte sums + codebook FMA, decode_frag_tc_from) and written with stmatrix into
+//        the K-major interleaved layout the MMA reads
+//   D  = fp32 accumulators in tensor memory (tcgen05.mma kind::f16, M=128, N=TN, K=16 per instruction). Long K sums
 //        are kept short: gate/up split K=6144 over 3 tiles (partial sums added in order in fp32 by the epilogue
-//        kernel), and inside a tile 128-input block b accumulates into chain b % 4 of tensor memory, the chains added
-//        in order in fp32 by the epilogue warps. With chains of at most 32 MMAs the tensor-core rounding stays within
-//        the EXACT-mode accuracy of the reference's fp32 kernel.
+//        kernel), and inside a tile 128-input block b accumulates into chain b % (512 / TN) of tensor memory, the chains
+//        added in order in fp32 by the epilogue warps. With chains of at most 64 MMAs the tensor-core rounding stays
+//        within the EXACT-mode accuracy of the reference's fp32 kernel.
 //
 // Warp roles: 0 producer (one lane issues the TMA / bulk copies), 1 MMA issuer (one lane) and tensor-memory owner,
-// 2..9 decoders (warp d owns n-tile d of the block), 10..13 epilogue (one tensor-memory lane quarter each: raw fp32
+// 2..9 decoders (warp d owns n-tiles d, d+8 of the block), 10..13 epilogue (one tensor-memory lane quarter each: raw fp32
 // D rows to global). Every wait is bounded; a timeout sets the workspace error word and all roles leave their loops,
 // drain their asynchronous work and free the tensor memory.
 //
@@ -31,28 +32,30 @@ namespace glmx {
 namespace {
 
 constexpr int PM = 128;                  // rows per tile (UMMA M)
-constexpr int PN = 128;                  // output columns per tile and projection (UMMA N)
 constexpr int PK = 64;                   // k per stage (4 UMMA K16 steps, 4 trellis k-rows)
 constexpr int NDEC = 8, NEPI = 4;
 constexpr int W_PROD = 0, W_MMA = 1, W_DEC0 = 2, W_EPI0 = W_DEC0 + NDEC;
 constexpr int PTHREADS = (W_EPI0 + NEPI) * 32;
 constexpr int SMEM_MAX = 227 * 1024;
 // kind::f16 instruction descriptor: D f32 (bit 4), A = B = f16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t) (PN >> 3) << 17) | ((uint32_t) (PM >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f16(int n) { return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (PM >> 4) << 24); }
 
-template <int K>
+// TN: output columns per tile (UMMA N): 256 where the projection's width allows it (each activation tile read from
+// L2 then feeds 256 FLOP per byte), else 128
+template <int K, int TN>
 struct CfgP
 {
+    static constexpr int NT = TN / 16;                  // trellis n-tiles per column block
     static constexpr int TA = PM * PK * 2;              // A tile bytes
-    static constexpr int TB = PN * PK * 2;              // decoded B tile bytes
-    static constexpr int TT = 4 * 8 * 32 * K;           // trellis bytes per stage: 4 k-rows x 8 tiles
+    static constexpr int TB = TN * PK * 2;              // decoded B tile bytes
+    static constexpr int TT = 4 * NT * 32 * K;          // trellis bytes per stage: 4 k-rows x NT tiles
     static constexpr int STAGE = TA + TB + TT;
     static constexpr int BAR_BYTES = 512;
     static constexpr int NST_FIT = (SMEM_MAX - 1024 - BAR_BYTES) / STAGE;
     static constexpr int NST = NST_FIT > 8 ? 8 : NST_FIT;
     static constexpr int SMEM = 1024 + NST * STAGE + BAR_BYTES;   // 1024: alignment slack of the swizzled A tiles
     static constexpr int TMEM_COLS = 512;
-    static constexpr int CH = TMEM_COLS / PN;                      // accumulator chains
+    static constexpr int CH = TMEM_COLS / TN;                      // accumulator chains
     static_assert(STAGE % 1024 == 0, "A tiles must stay 1024-byte aligned");
     static_assert(NST >= 2, "at least two stages");
     static_assert(SMEM <= SMEM_MAX, "shared memory");
@@ -102,6 +105,7 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // 16 consecutive fp32 columns of this thread's tensor-memory lane (32x32b shape: warp quarter q reads lanes 32q..32q+31)
+// (the registers are valid after tmem_wait_ld)
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
 {
     asm volatile(
@@ -109,8 +113,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
           "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
 {
@@ -148,11 +153,11 @@ __device__ __forceinline__ PfTile pf_tile(long long t, int NB, int NP, int KS)
     return r;
 }
 
-template <int K>
+template <int K, int TN>
 __global__ void __launch_bounds__(PTHREADS, 1)
     gemm_pf_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1, PfArgs a)
 {
-    using C = CfgP<K>;
+    using C = CfgP<K, TN>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -188,7 +193,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     const uint32_t tmem = *tmem_slot;
 
     const int J = a.plan->J;
-    const int NB = a.ndim / PN, NP = a.nproj, KS = a.ksplit;
+    const int NB = a.ndim / TN, NP = a.nproj, KS = a.ksplit;
     const long long ntiles = (long long) J * NB * NP * KS;
     const int nks = a.kt / 4 / KS;            // stages per tile (this tile's share of K)
     auto stage = [&](int s) { return smem + (size_t) s * C::STAGE; };
@@ -217,8 +222,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                     tma_load_2d(st, map, kg * PK, job.y, &full[s]);
 #pragma unroll
                     for (int r = 0; r < 4; ++r)
-                        bulk_g2s(st + C::TA + C::TB + r * 8 * 32 * K, b + ((size_t) (kg * 4 + r) * a.ntn + tl.nb * 8) * (32 * K),
-                                 8 * 32 * K, &full[s]);
+                        bulk_g2s(st + C::TA + C::TB + r * C::NT * 32 * K,
+                                 b + ((size_t) (kg * 4 + r) * a.ntn + tl.nb * C::NT) * (32 * K), C::NT * 32 * K, &full[s]);
                 }
             }
             // every issued copy lands before the CTA may exit
@@ -254,8 +259,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                     const uint32_t sa = smem_u32(st), sb = smem_u32(st + C::TA);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_f16(tmem + (uint32_t) (ch * PN), umma_desc(sa + kk * 32, 16, 1024, 2),
-                                 umma_desc(sb + kk * 256, 128, 1024, 0), IDESC, acc || kk != 0);
+                        umma_f16(tmem + (uint32_t) (ch * TN), umma_desc(sa + kk * 32, 16, 1024, 2),
+                                 umma_desc(sb + kk * 256, 128, 1024, 0), idesc_f16(TN), acc || kk != 0);
                     umma_commit(&empty[s]);
                 }
                 if (!ok) break;
@@ -268,7 +273,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     }
     else if (warp < W_EPI0)
     {
-        // decoders: warp d owns n-tile d of the 128-column block; per stage it decodes its 4 k-tiles
+        // decoders: warp d owns n-tiles d, d + 8, ... of the column block; per stage it decodes their 4 k-tiles
+        constexpr int NPW = C::NT / NDEC;              // n-tiles per decoder warp
         const int d = warp - W_DEC0;
         LaneDecode<K> L;
         L.init(lane);
@@ -276,8 +282,14 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         ones.init(lane);
         // stmatrix row address of this lane: matrix j = lane / 8 (0: n 0-7 k 0-7, 1: n 8-15 k 0-7, 2: n 0-7 k 8-15,
         // 3: n 8-15 k 8-15), row = lane % 8; K-major interleaved B: 8-row groups 1024 B apart, 16-byte k-chunks 128 B
-        const int j = lane >> 3, n = 16 * d + (lane & 7) + 8 * (j & 1);
-        const uint32_t boff = (uint32_t) ((n >> 3) * 1024 + (j >> 1) * 128 + (n & 7) * 16);
+        const int j = lane >> 3;
+        uint32_t boff[NPW];
+#pragma unroll
+        for (int i = 0; i < NPW; ++i)
+        {
+            const int n = 16 * (d + NDEC * i) + (lane & 7) + 8 * (j & 1);
+            boff[i] = (uint32_t) ((n >> 3) * 1024 + (j >> 1) * 128 + (n & 7) * 16);
+        }
         long long it = 0;
         for (long long t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x)
         {
@@ -289,14 +301,24 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                 if (s_abort) break;
                 uint8_t* st = stage(s);
                 const uint8_t* tr = st + C::TA + C::TB;
-                const uint32_t sb = smem_u32(st + C::TA) + boff;
+                const uint32_t sb = smem_u32(st + C::TA);
+                // all loads first, then independent decode chains, then the stores
+                uint32_t hw[4 * NPW], lw[4 * NPW], frag[4 * NPW][4];
 #pragma unroll
-                for (int kt = 0; kt < 4; ++kt)
-                {
-                    uint32_t frag[4];
-                    decode_frag_tc<K>(tr + (kt * 8 + d) * (32 * K), L, ones, frag);
-                    stmatrix_x4(sb + kt * 256, frag);
-                }
+                for (int i = 0; i < NPW; ++i)
+#pragma unroll
+                    for (int kt = 0; kt < 4; ++kt)
+                    {
+                        const uint8_t* tile = tr + (kt * C::NT + d + NDEC * i) * (32 * K);
+                        hw[i * 4 + kt] = lds32(tile + L.off_hi);
+                        lw[i * 4 + kt] = lds32(tile + L.off_lo);
+                    }
+#pragma unroll
+                for (int u = 0; u < 4 * NPW; ++u) decode_frag_tc_from<K>(hw[u], lw[u], L, ones, frag[u]);
+#pragma unroll
+                for (int i = 0; i < NPW; ++i)
+#pragma unroll
+                    for (int kt = 0; kt < 4; ++kt) stmatrix_x4(sb + boff[i] + kt * 256, frag[i * 4 + kt]);
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&dec[s]);
@@ -318,22 +340,28 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             const int r = 32 * q + lane;
             const bool valid = r < job.z;
             const size_t row = (size_t) job.y + r;
-            for (int c = 0; c < PN / 16; ++c)
+            const uint32_t tq = tmem + ((uint32_t) (32 * q) << 16);
+            for (int c = 0; c < TN / 16; ++c)
             {
-                uint32_t v[16];
+                // the chains' 16 columns are loaded together and waited for once, then added in chain order
+                uint32_t v[C::CH][16];
+#pragma unroll
+                for (int ch = 0; ch < C::CH; ++ch)
+                    if (ch < chains) tmem_ld16(tq + (uint32_t) (ch * TN + c * 16), v[ch]);
+                tmem_wait_ld();
                 float f[16];
-                tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (c * 16), v);
 #pragma unroll
-                for (int u = 0; u < 16; ++u) f[u] = __uint_as_float(v[u]);
-                for (int ch = 1; ch < chains; ++ch)
-                {
-                    tmem_ld16(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (ch * PN + c * 16), v);
+                for (int u = 0; u < 16; ++u) f[u] = __uint_as_float(v[0][u]);
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) f[u] = __fadd_rn(f[u], __uint_as_float(v[u]));
-                }
+                for (int ch = 1; ch < C::CH; ++ch)
+                    if (ch < chains)
+                    {
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) f[u] = __fadd_rn(f[u], __uint_as_float(v[ch][u]));
+                    }
                 if (valid)
                 {
-                    float4* dst = reinterpret_cast<float4*>(yout + (row * a.nslot + a.slot0 + tl.p) * a.ndim + tl.nb * PN + c * 16);
+                    float4* dst = reinterpret_cast<float4*>(yout + (row * a.nslot + a.slot0 + tl.p) * a.ndim + tl.nb * TN + c * 16);
 #pragma unroll
                     for (int u = 0; u < 4; ++u) dst[u] = make_float4(f[4 * u], f[4 * u + 1], f[4 * u + 2], f[4 * u + 3]);
                 }
@@ -445,16 +473,16 @@ cudaError_t act_map(CUtensorMap* m, const void* base, int kdim, int rows)
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int K>
+template <int K, int TN>
 cudaError_t launch_gemm_pf(const Layer& L, const CUtensorMap& m0, const CUtensorMap& m1, const PfArgs& a, long long max_tiles,
                            cudaStream_t st)
 {
-    using C = CfgP<K>;
+    using C = CfgP<K, TN>;
     static bool attr_set[64] = {};
     static int sms[64] = {};
     if (!attr_set[L.device])
     {
-        cudaError_t e = cudaFuncSetAttribute(gemm_pf_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_pf_kernel<K, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         if (cudaDeviceGetAttribute(&sms[L.device], cudaDevAttrMultiProcessorCount, L.device) != cudaSuccess || sms[L.device] <= 0)
             sms[L.device] = 148;
@@ -462,18 +490,31 @@ cudaError_t launch_gemm_pf(const Layer& L, const CUtensorMap& m0, const CUtensor
     }
     const long long grid = max_tiles < sms[L.device] ? max_tiles : sms[L.device];
     if (grid <= 0) return cudaSuccess;
-    gemm_pf_kernel<K><<<(unsigned) grid, PTHREADS, C::SMEM, st>>>(m0, m1, a);
+    gemm_pf_kernel<K, TN><<<(unsigned) grid, PTHREADS, C::SMEM, st>>>(m0, m1, a);
     return cudaGetLastError();
 }
 
+// tile width for a projection of width n
+int pf_tile_n(int n) { return n % 256 == 0 ? 256 : 128; }
+
+// one launch over jobs_max x (ndim / TN) x per_job tiles (per_job: projections x K splits)
 cudaError_t launch_gemm_pf_bits(const Layer& L, int bits, const CUtensorMap& m0, const CUtensorMap& m1, const PfArgs& a,
-                                long long max_tiles, cudaStream_t st)
+                                long long jobs_max, long long per_job, cudaStream_t st)
 {
+    const int tn = pf_tile_n(a.ndim);
+    const long long mt = jobs_max * (a.ndim / tn) * per_job;
+    if (tn == 256)
+        switch (bits)
+        {
+            case 2: return launch_gemm_pf<2, 256>(L, m0, m1, a, mt, st);
+            case 3: return launch_gemm_pf<3, 256>(L, m0, m1, a, mt, st);
+            default: return launch_gemm_pf<4, 256>(L, m0, m1, a, mt, st);
+        }
     switch (bits)
     {
-        case 2: return launch_gemm_pf<2>(L, m0, m1, a, max_tiles, st);
-        case 3: return launch_gemm_pf<3>(L, m0, m1, a, max_tiles, st);
-        default: return launch_gemm_pf<4>(L, m0, m1, a, max_tiles, st);
+        case 2: return launch_gemm_pf<2, 128>(L, m0, m1, a, mt, st);
+        case 3: return launch_gemm_pf<3, 128>(L, m0, m1, a, mt, st);
+        default: return launch_gemm_pf<4, 128>(L, m0, m1, a, mt, st);
     }
 }
 
@@ -514,15 +555,15 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
         g.yraw = reinterpret_cast<float*>(ws + lay.yraw_gu);
         if (L.bits[0] == L.bits[1])
         {
-            if ((e = launch_gemm_pf_bits(L, L.bits[0], mg, mu, g, jobs_max * (L.I / PN) * 2 * g.ksplit, st)) != cudaSuccess) return e;
+            if ((e = launch_gemm_pf_bits(L, L.bits[0], mg, mu, g, jobs_max, 2 * g.ksplit, st)) != cudaSuccess) return e;
         }
         else
         {   // gate and up at different trellis widths: one launch each
             PfArgs g1 = g;
             g1.nproj = 1;
-            if ((e = launch_gemm_pf_bits(L, L.bits[0], mg, mg, g1, jobs_max * (L.I / PN) * g.ksplit, st)) != cudaSuccess) return e;
+            if ((e = launch_gemm_pf_bits(L, L.bits[0], mg, mg, g1, jobs_max, g.ksplit, st)) != cudaSuccess) return e;
             g1.proj0 = 1; g1.slot0 = 1;
-            if ((e = launch_gemm_pf_bits(L, L.bits[1], mu, mu, g1, jobs_max * (L.I / PN) * g.ksplit, st)) != cudaSuccess) return e;
+            if ((e = launch_gemm_pf_bits(L, L.bits[1], mu, mu, g1, jobs_max, g.ksplit, st)) != cudaSuccess) return e;
         }
 
         EpiPfArgs q;
@@ -543,7 +584,7 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
         d.proj0 = 2; d.nproj = 1; d.nslot = 1; d.slot0 = 0; d.kt = L.I / 16; d.ntn = L.H / 16; d.ndim = L.H;
         d.ksplit = 1; d.split_stride = 0;
         d.yraw = reinterpret_cast<float*>(ws + lay.yrow);
-        if ((e = launch_gemm_pf_bits(L, L.bits[2], md, md, d, jobs_max * (L.H / PN), st)) != cudaSuccess) return e;
+        if ((e = launch_gemm_pf_bits(L, L.bits[2], md, md, d, jobs_max, 1, st)) != cudaSuccess) return e;
         if ((e = mark(4)) != cudaSuccess) return e;
     }
     else
