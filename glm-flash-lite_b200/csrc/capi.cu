@@ -165,9 +165,12 @@ int glmx_moe_forward(const glmx_layer* l, const void* x, int x_dtype, int ntok, 
                                   ws_bytes, stream, nullptr);
 }
 
-int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
-                           const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate, void* ws,
-                           size_t ws_bytes, void* stream, void* const* events)
+}  // extern "C"
+
+// the forward of glmx_moe_forward_timed and glmx_moe_forward_hc (hc: hyper-connection epilogue instead of `out`)
+static int forward_impl(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                        const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate, void* ws,
+                        size_t ws_bytes, void* stream, void* const* events, const HcOut* hc)
 {
     WsLayout lay;
     int grid;
@@ -188,7 +191,7 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     if (x_dtype != GLMX_F16 && x_dtype != GLMX_F32 && x_dtype != GLMX_BF16)
         return fail(GLMX_E_ARG, "glmx_moe_forward: x dtype must be fp16, fp32 or bf16");
     if (out_dtype != GLMX_F16 && out_dtype != GLMX_F32) return fail(GLMX_E_ARG, "glmx_moe_forward: out dtype must be fp16 or fp32");
-    if (ntok > 0 && (!x || !out)) return fail(GLMX_E_ARG, "glmx_moe_forward: null x/out");
+    if (ntok > 0 && (!x || (!out && !hc))) return fail(GLMX_E_ARG, "glmx_moe_forward: null x/out");
     if (ntok * topk > 0 && (!sel || !w)) return fail(GLMX_E_ARG, "glmx_moe_forward: null sel/w");
     if (out && !aligned16(out)) return fail(GLMX_E_ARG, "glmx_moe_forward: out must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -200,13 +203,34 @@ int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int 
     if (e == cudaSuccess && events && events[1]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[1]), st);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: route launch");
     if (base == GLMX_MODE_I16)
-        e = launch_i16_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events);
+        e = launch_i16_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events, hc);
     else if (gemm)
-        e = launch_prefill_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events);
+        e = launch_prefill_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events, hc);
     else
-        e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, base, out, out_dtype, accumulate, wsb, lay, grid, st, events);
+        e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, base, out, out_dtype, accumulate, wsb, lay, grid, st, events, hc);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: launch");
     return GLMX_OK;
+}
+
+extern "C" {
+
+int glmx_moe_forward_timed(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                           const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate, void* ws,
+                           size_t ws_bytes, void* stream, void* const* events)
+{
+    return forward_impl(l, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, out, out_dtype, accumulate, ws, ws_bytes,
+                        stream, events, nullptr);
+}
+
+int glmx_moe_forward_hc(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                        const void* w, int w_dtype, int topk, int mode, float* hc_x, const float* hc_post,
+                        const float* hc_comb, int y_dtype, void* ws, size_t ws_bytes, void* stream)
+{
+    if (ntok > 0 && (!hc_x || !hc_post || !hc_comb)) return fail(GLMX_E_ARG, "glmx_moe_forward_hc: null stream stack / post / comb");
+    if (y_dtype != GLMX_F16 && y_dtype != GLMX_F32) return fail(GLMX_E_ARG, "glmx_moe_forward_hc: y dtype must be fp16 or fp32");
+    const HcOut hc{ hc_x, hc_post, hc_comb, y_dtype == GLMX_F16 ? 1 : 0 };
+    return forward_impl(l, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, nullptr, GLMX_F32, 0, ws, ws_bytes, stream,
+                        nullptr, &hc);
 }
 
 int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, void* stream)

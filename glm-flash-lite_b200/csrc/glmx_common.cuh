@@ -226,6 +226,24 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// ---- hyper-connection update of one column (exllamav3 hc_apply; glm53/k_hcfuse.py:62-91) --------------------------
+// x_row: the row's 4 streams [4][D]; x_g <- post_g * y + comb[0][g] * x_0 + ... + comb[3][g] * x_3, the products
+// accumulated by fma in stream order h = 0..3 starting from post_g * y (the reference's expressions and order).
+__device__ __forceinline__ void hc_apply_col(float* x_row, int D, int c, float y, const float* post, const float* comb)
+{
+    float xv[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) xv[h] = x_row[(size_t) h * D + c];
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+    {
+        float o = __fmul_rn(post[g], y);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) o = __fmaf_rn(comb[h * 4 + g], xv[h], o);
+        x_row[(size_t) g * D + c] = o;
+    }
+}
+
 // ---- 128-point transforms on one warp (lane holds v[q] = element lane + 32 q) ------------------------------------------
 
 // Unnormalised Walsh-Hadamard butterfly in the reference's stage order w = 1, 2, ..., 64 (ft_core.h:89-94):

@@ -53,23 +53,35 @@ int gemv_grid_ctas(const Layer& L);
 
 void set_error(const std::string& msg);
 
+// Hyper-connection epilogue of the combine (exllamav3 hc_apply as glm53/k_hcfuse.py:62-91 restates it): instead of
+// writing the layer output y, update the row's stream stack in place, x_g <- post_g * y + sum_h comb[h][g] * x_h.
+struct HcOut
+{
+    float* x;              // [ntok][4][H] fp32 stream stack, updated in place
+    const float* post;     // [ntok][4]
+    const float* comb;     // [ntok][4][4], comb[h][g]
+    int y_half;            // 1: y is rounded to fp16 first (an fp16 sublayer output), 0: fp32
+};
+
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
                          int maxm, uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);
 cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,
                                   int out_dtype, int accumulate, uint8_t* ws, const WsLayout& lay, int grid_ctas,
-                                  cudaStream_t st, void* const* events);
+                                  cudaStream_t st, void* const* events, const HcOut* hc = nullptr);
 cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
-                               int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events);
+                               int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events,
+                               const HcOut* hc = nullptr);
 cudaError_t launch_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, cudaStream_t st);
 // prefill path (tensor-core GEMM, EXACT mode) and the two kernels it shares with the GEMV paths
 cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
-                                   int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events);
+                                   int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events,
+                                   const HcOut* hc = nullptr);
 // EXACT input transform of every row (xg, xu: fp16 [R][H], PERM16 order)
 cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st);
 // down out_block of raw fp32 rows [R][H] + weighted sum in pick order (+ shared expert) into out
 cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
-                               uint8_t* ws, const WsLayout& lay, cudaStream_t st);
+                               uint8_t* ws, const WsLayout& lay, cudaStream_t st, const HcOut* hc = nullptr);
 
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)

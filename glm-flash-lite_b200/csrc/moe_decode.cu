@@ -350,6 +350,7 @@ struct CombineArgs
     const int* pick_row; const float* row_weight; const float* y;
     int H, ntok, topk, has_shared;
     void* out; int out_dtype; int accumulate;
+    HcOut hc;                           // hc.x != nullptr: hyper-connection epilogue instead of writing out
 };
 
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
@@ -374,6 +375,15 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
         const int r = a.plan->P + t;
         const float4 y = *reinterpret_cast<const float4*>(a.y + (size_t) r * a.H + c);
         acc.x = __fadd_rn(acc.x, y.x); acc.y = __fadd_rn(acc.y, y.y); acc.z = __fadd_rn(acc.z, y.z); acc.w = __fadd_rn(acc.w, y.w);
+    }
+    if (a.hc.x)
+    {
+        const float v[4] = { acc.x, acc.y, acc.z, acc.w };
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            hc_apply_col(a.hc.x + (size_t) t * 4 * a.H, a.H, c + i, a.hc.y_half ? __half2float(__float2half_rn(v[i])) : v[i],
+                         a.hc.post + (size_t) t * 4, a.hc.comb + (size_t) t * 16);
+        return;
     }
     const size_t o = (size_t) t * a.H + c;
     if (a.out_dtype == GLMX_F32)
@@ -547,7 +557,7 @@ cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_
 
 cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,
                                   int out_dtype, int accumulate, uint8_t* ws, const WsLayout& lay, int grid, cudaStream_t st,
-                                  void* const* events)
+                                  void* const* events, const HcOut* hc)
 {
     (void) mode;
     auto mark = [&](int i) -> cudaError_t {
@@ -615,6 +625,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
         c.y = reinterpret_cast<const float*>(ws + lay.yrow);
         c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared;
         c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
+        c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
         dim3 grd((unsigned) ((L.H / 4 + 255) / 256), (unsigned) ntok);
         combine_kernel<<<grd, 256, 0, st>>>(c);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;

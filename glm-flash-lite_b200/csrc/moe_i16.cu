@@ -360,6 +360,7 @@ struct CombineI16Args
     const __half* svh_d;
     int H, ntok, topk, has_shared, E;
     void* out; int out_dtype; int accumulate;
+    HcOut hc;                           // hc.x != nullptr: hyper-connection epilogue instead of writing out
 };
 
 // one warp per (token, 128-output block): down out_block per pick, weighted sum in pick order (+ shared)
@@ -396,6 +397,17 @@ __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
             const float yq = r16(__fmul_rn(__fmul_rn(y[q], HAD), __half2float(a.svh_d[(size_t) e * a.H + c])));
             acc[q] = k < a.topk ? __fadd_rn(acc[q], __fmul_rn(w, yq)) : __fadd_rn(acc[q], yq);
         }
+    }
+    if (a.hc.x)
+    {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+        {
+            const float y = a.hc.y_half ? __half2float(__float2half_rn(acc[q])) : acc[q];
+            hc_apply_col(a.hc.x + (size_t) t * 4 * a.H, a.H, hb * 128 + lane + 32 * q, y, a.hc.post + (size_t) t * 4,
+                         a.hc.comb + (size_t) t * 16);
+        }
+        return;
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q)
@@ -446,7 +458,7 @@ cudaError_t launch_gu_i16_k0(const Layer& L, const GemvI16Args& a, cudaStream_t 
 }  // namespace
 
 cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
-                               uint8_t* ws, const WsLayout& lay, cudaStream_t st)
+                               uint8_t* ws, const WsLayout& lay, cudaStream_t st, const HcOut* hc)
 {
     if (ntok <= 0) return cudaSuccess;
     CombineI16Args c;
@@ -458,13 +470,15 @@ cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int 
     c.svh_d = reinterpret_cast<const __half*>(L.svh[2]);
     c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared; c.E = L.E;
     c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
+    c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
     const long long w3 = (long long) ntok * (L.H / 128);
     combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
     return cudaGetLastError();
 }
 
 cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
-                               int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events)
+                               int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events,
+                               const HcOut* hc)
 {
     auto mark = [&](int i) -> cudaError_t {
         if (events && events[i]) return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -553,6 +567,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         c.svh_d = reinterpret_cast<const __half*>(L.svh[2]);
         c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared; c.E = L.E;
         c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
+        c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
         const long long w3 = (long long) ntok * (L.H / 128);
         combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -521,7 +521,8 @@ cudaError_t launch_gemm_pf_bits(const Layer& L, int bits, const CUtensorMap& m0,
 }  // namespace
 
 cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
-                                   int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events)
+                                   int accumulate, uint8_t* ws, const WsLayout& lay, cudaStream_t st, void* const* events,
+                                   const HcOut* hc)
 {
     auto mark = [&](int i) -> cudaError_t {
         if (events && events[i]) return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -594,7 +595,7 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
     }
     if (ntok > 0)
         if ((e = launch_combine_raw(L, reinterpret_cast<const float*>(ws + lay.yrow), ntok, topk, out, out_dtype, accumulate, ws,
-                                    lay, st)) != cudaSuccess)
+                                    lay, st, hc)) != cudaSuccess)
             return e;
     return mark(5);
 }

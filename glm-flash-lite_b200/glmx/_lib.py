@@ -37,7 +37,7 @@ class GlmxError(RuntimeError):
 # every symbol include/glmx.h declares
 EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_destroy", "glmx_layer_set_act_limit",
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
-           "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc")
+           "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc")
 NOALLOC_SCRATCH_BYTES = 48 << 20
 
 _lib = None
@@ -75,6 +75,8 @@ def load(path: str = LIB_PATH):
     L.glmx_check.restype = _I
     L.glmx_moe_forward_noalloc.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I, _P]
     L.glmx_moe_forward_noalloc.restype = _I
+    L.glmx_moe_forward_hc.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _I, _P, C.c_size_t, _P]
+    L.glmx_moe_forward_hc.restype = _I
     if L.glmx_version() != ABI_VERSION:
         raise RuntimeError(f"libglmx ABI {L.glmx_version()} != {ABI_VERSION}")
     _lib = L

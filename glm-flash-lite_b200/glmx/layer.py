@@ -170,6 +170,26 @@ class MoELayer:
                                               ws.data_ptr(), ws.numel(), _stream_ptr(stream), ev))
         return out
 
+    def forward_hc(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, hc_x: torch.Tensor, post: torch.Tensor,
+                   comb: torch.Tensor, y_half: bool = True, mode: int = _lib.MODE_I16, stream=None) -> torch.Tensor:
+        """The layer followed by the hyper-connection update of the MoE site (glmx_moe_forward_hc): hc_x fp32
+        [ntok, 4, H] is updated in place with x_g <- post_g * y + sum_h comb[h][g] * x_h (y = the layer output, rounded
+        to fp16 first when y_half); post fp32 [ntok, 4], comb fp32 [ntok, 4, 4]. Returns hc_x."""
+        x = x.contiguous(); sel = sel.contiguous(); w = w.contiguous()
+        ntok = x.shape[0]
+        topk = sel.shape[1] if sel.dim() == 2 else 0
+        if hc_x.shape != (ntok, 4, self.H) or hc_x.dtype != torch.float32 or not hc_x.is_contiguous():
+            raise ValueError("hc_x must be contiguous fp32 [ntok, 4, H]")
+        post = post.to(torch.float32).contiguous(); comb = comb.to(torch.float32).contiguous()
+        if post.shape != (ntok, 4) or comb.shape != (ntok, 4, 4):
+            raise ValueError("post must be [ntok, 4] and comb [ntok, 4, 4]")
+        ws = self.workspace(ntok, topk)
+        check(self.lib.glmx_moe_forward_hc(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
+                                           _dt(w), topk, int(mode), hc_x.data_ptr(), post.data_ptr(), comb.data_ptr(),
+                                           _lib.F16 if y_half else _lib.F32, ws.data_ptr(), ws.numel(),
+                                           _stream_ptr(stream)))
+        return hc_x
+
     def check_device(self, ntok: int, topk: int, stream=None) -> int:
         """Synchronise and read the device error word of the last call (0 = fine)."""
         flags = C.c_int(0)

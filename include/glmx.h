@@ -115,6 +115,18 @@ GLMX_API int glmx_moe_forward_timed(const glmx_layer* layer, const void* x, int 
                      int sel_dtype, const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
                      void* workspace, size_t workspace_bytes, void* stream, void* const* events);
 
+/* glmx_moe_forward followed, in the combine kernel itself, by the hyper-connection update that comes right after the
+ * MoE sublayer in GLM-5.3 (exllamav3 hc_apply, fused by the reference into k_apply_partials: glm53/k_hcfuse.py:62-91):
+ * for every token t and column c, with y the layer output (rounded to fp16 first when y_dtype is GLMX_F16, as an fp16
+ * sublayer output is) and x the token's 4-stream stack,
+ *     x[t][g][c] <- post[t][g] * y + comb[t][0][g] * x[t][0][c] + ... + comb[t][3][g] * x[t][3][c]   (g = 0..3)
+ * with the products added by fma in stream order (the reference's expressions). hc_x: device fp32 [ntok][4][H],
+ * updated in place; hc_post: fp32 [ntok][4]; hc_comb: fp32 [ntok][4][4] (comb[h][g]). The layer output itself is not
+ * written. Same modes, paths and workspace as glmx_moe_forward. */
+GLMX_API int glmx_moe_forward_hc(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
+                     int sel_dtype, const void* w, int w_dtype, int topk, int mode, float* hc_x, const float* hc_post,
+                     const float* hc_comb, int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Known-answer entry for the trellis decode: `ntiles` tiles of 32*bits bytes (device) -> fp16 bit patterns
  * [ntiles, 16, 16] (row r = input index, column c = output index), as dense_weights (kernels/cpu_avx2/ft_core.h:1657-1672). */
 GLMX_API int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, void* stream);

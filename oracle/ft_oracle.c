@@ -353,3 +353,22 @@ void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* sha
     }
     free(ysh); free(xs); free(yrow); free(pick_row); free(row_pick); free(row_weight); free(row_token); free(offsets);
 }
+
+/* glm53/k_hcfuse.py:62-91 (k_apply_partials, APPLY leg): o = post_g * y, then o = fmaf(comb[h][g], x_h, o), h = 0..3 */
+void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, const float* comb)
+{
+    for (int r = 0; r < R; ++r)
+        for (int c = 0; c < D; ++c)
+        {
+            float* xr = x + (size_t) r * 4 * D;
+            float xv[4];
+            for (int h = 0; h < 4; ++h) xv[h] = xr[(size_t) h * D + c];
+            const float yv = y[(size_t) r * D + c];
+            for (int g = 0; g < 4; ++g)
+            {
+                float o = post[r * 4 + g] * yv;
+                for (int h = 0; h < 4; ++h) o = fmaf(comb[(r * 4 + h) * 4 + g], xv[h], o);
+                xr[(size_t) g * D + c] = o;
+            }
+        }
+}

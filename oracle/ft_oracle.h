@@ -86,6 +86,11 @@ void fto_expert_i16(const fto_expert_t* ex, int H, int I, float act_limit, const
 void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* shared, int H, int I, int mode,
                      float act_limit, const float* x, int ntok, const int32_t* sel, const float* w, int topk, float* out);
 
+/* Hyper-connection update after the MoE sublayer (exllamav3 hc_apply as glm53/k_hcfuse.py:62-91 restates it):
+ * x [R][4][D] fp32 updated in place, y [R][D] the sublayer output (already in the precision the model feeds it),
+ * post [R][4], comb [R][4][4] (comb[h][g]): x_g <- fma(comb[3][g], x_3, ... fma(comb[0][g], x_0, post_g * y)). */
+void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, const float* comb);
+
 #ifdef __cplusplus
 }
 #endif

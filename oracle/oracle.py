@@ -65,6 +65,7 @@ class Oracle:
         L.fto_jobs_ref.argtypes = [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]
         L.fto_moe_forward.argtypes = [_P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P, _I, _P]
         L.fto_expert_i16.argtypes = [_P, _I, _I, _F, _P, _I, _P]
+        L.fto_hc_apply.argtypes = [_P, _P, _I, _I, _P, _P]
         L.fto_init()
         self.L = L
 
@@ -86,6 +87,14 @@ class Oracle:
         return int(self.L.fto_state(_ptr(np.ascontiguousarray(tile)), K, t))
 
     # --- transforms ------------------------------------------------------------------------------------------
+    def hc_apply(self, x: np.ndarray, y: np.ndarray, post: np.ndarray, comb: np.ndarray) -> np.ndarray:
+        """Hyper-connection update (fto_hc_apply): returns the new stream stack [R, 4, D] fp32."""
+        x = np.array(x, np.float32, copy=True, order="C")
+        R, _, D = x.shape
+        self.L.fto_hc_apply(_ptr(x), _ptr(np.ascontiguousarray(y, np.float32)), R, D,
+                            _ptr(np.ascontiguousarray(post, np.float32)), _ptr(np.ascontiguousarray(comb, np.float32)))
+        return x
+
     def prep_block(self, x: np.ndarray, suh: np.ndarray) -> np.ndarray:
         xt = np.empty(128, np.float32)
         self.L.fto_prep_block(_ptr(np.ascontiguousarray(x, np.float32)), _ptr(np.ascontiguousarray(suh, np.float16)), _ptr(xt))

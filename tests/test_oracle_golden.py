@@ -85,3 +85,18 @@ def test_i16_restatement_bit_exact_vs_reference(oracle):
     got = oracle.moe_forward(b, d["multi_x"], d["multi_sel"], d["multi_w"], mode=2)
     mx, rr = parity(got, d["multi_i16"])
     assert mx < 1e-6 and rr < 1e-7, (mx, rr)
+
+
+def test_hc_apply_restatement(oracle):
+    """fto_hc_apply against the same update in float64 (it differs only by fp32 rounding of each fma step)."""
+    rng = np.random.default_rng(3)
+    R, D = 3, 64
+    x = rng.standard_normal((R, 4, D)).astype(np.float32)
+    y = rng.standard_normal((R, D)).astype(np.float32)
+    post = rng.random((R, 4)).astype(np.float32)
+    comb = rng.standard_normal((R, 4, 4)).astype(np.float32)
+    got = oracle.hc_apply(x, y, post, comb)
+    want = post.astype(np.float64)[:, :, None] * y.astype(np.float64)[:, None, :] + \
+        np.einsum("rhg,rhd->rgd", comb.astype(np.float64), x.astype(np.float64))
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(x, oracle.hc_apply(x, y, post, comb) * 0 + x)      # input untouched
