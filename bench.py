@@ -182,6 +182,84 @@ def run_reference_impl(args, rank, world):
 
 
 # ------------------------------------------------------------------------------------------------------------------
+def run_sweep(args, dev):
+    """mixed-bitrate and skew sweep on one layer (288 routed + shared, H=6144, I=1536). Bitrates (gate, up,
+    down) = (2,2,2), (3,3,3), (4,4,4), (4,4,2); decode B = 1, 8, 64 (I16) and prefill T = 512, 2048 (EXACT, the
+    path chosen by the library: the tensor-core GEMM from 12 rows per expert) under uniform, Zipf(0.8 / 1.1 / 1.5) and
+    hot-set (16 experts take 80 %) routing. Device time per call (CUDA
+    events, warm, L2 not flushed between calls: every configuration streams more than L2 except B=1)."""
+    import torch
+    from glmx import MoELayer, _lib, synth
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    et = E + 1
+    pk, pk_kind = peaks()
+    stream = torch.cuda.current_stream(dev)
+    results = []
+
+    def timed(layer, x, sel, w, mode, steps, warmup):
+        for i in range(warmup):
+            layer.forward(x, sel[i % len(sel)], w[i % len(w)], mode=mode)
+        torch.cuda.synchronize(dev)
+        t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            layer.forward(x, sel[i % len(sel)], w[i % len(w)], mode=mode)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        return t0.elapsed_time(t1) / steps
+
+    def routes(kind, ntok, n):
+        if kind == "uniform":
+            return [synth.route_uniform(ntok, E, TOPK, 3000 + i) for i in range(n)]
+        if kind.startswith("zipf"):
+            return [synth.route_zipf(ntok, E, TOPK, float(kind[4:]), 3100 + i) for i in range(n)]
+        return [synth.route_hotset(ntok, E, TOPK, 16, 0.8, 3200 + i) for i in range(n)]
+
+    for bits in ((2, 2, 2), (3, 3, 3), (4, 4, 4), (4, 4, 2)):
+        proj = [(H // 16) * (I // 16) * 32 * b for b in bits]
+        per = sum(proj)
+        tr = torch.randint(0, 256, (et * per,), dtype=torch.uint8, device=dev, generator=g)
+        ptrs = torch.tensor([[tr.data_ptr() + e * per + sum(proj[:p]) for p in range(3)] for e in range(et)], dtype=torch.int64)
+        sign = lambda shape: torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
+        suh = [sign((et, k)).half() for k in (H, H, I)]
+        svh = [(sign((et, m)) * (0.02 + 0.005 * torch.randn((et, m), device=dev, generator=g)).abs()).half() for m in (I, I, H)]
+        layer = MoELayer(H, I, E, ptrs, suh, svh, bits=bits, has_shared=True, keep=[tr], device=dev)
+        expert_bytes = per + SCALE_BYTES
+        for B in (1, 8, 64):
+            for kind in ("uniform", "zipf1.1", "hotset"):
+                rs = routes(kind, B, 8)
+                sel = [torch.from_numpy(a).to(dev) for a, _ in rs]
+                wts = [torch.from_numpy(b).to(dev) for _, b in rs]
+                x = torch.randn((B, H), device=dev, generator=g).half()
+                ms = timed(layer, x, sel, wts, _lib.MODE_I16, 20, 3)
+                touched = float(np.mean([np.unique(a).size + 1 for a, _ in rs]))
+                results.append({"bits": list(bits), "phase": "decode", "tokens": B, "routing": kind, "ms": ms,
+                                "tok_per_s": B / (ms / 1e3), "hbm_gbs": touched * expert_bytes / (ms / 1e3) / 1e9})
+        for T in (512, 2048):
+            for kind in ("uniform", "zipf1.1", "zipf1.5", "zipf0.8"):
+                rs = routes(kind, T, 2)
+                sel = [torch.from_numpy(a).to(dev) for a, _ in rs]
+                wts = [torch.from_numpy(b).to(dev) for _, b in rs]
+                x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+                ms = timed(layer, x, sel, wts, _lib.MODE_EXACT, 3, 2)            # the library picks GEMV or GEMM
+                flop = 2.0 * 3 * H * I * T * (TOPK + 1)
+                results.append({"bits": list(bits), "phase": "prefill", "tokens": T, "routing": kind, "ms": ms,
+                                "tok_per_s": T / (ms / 1e3), "tflops": flop / (ms / 1e3) / 1e12})
+        del layer, tr
+        torch.cuda.empty_cache()
+    head = next(r for r in results if r["bits"] == [3, 3, 3] and r["phase"] == "decode" and r["tokens"] == 64
+                and r["routing"] == "uniform")
+    line = {"metric": "moe_layer_decode_tok_per_s", "value": head["tok_per_s"], "unit": "tok/s", "n_gpus": 1,
+            "steps": 20, "warmup": 3, "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int16-act/int32-acc (decode), fp16/fp32-acc (prefill)", "data": "synthetic",
+            "config": {"workload": "configs[4] mixed-bitrate and skew sweep (value: the K=3 uniform B=64 entry)",
+                       "H": H, "I": I, "experts": E, "shared": 1, "topk": TOPK},
+            "peak_hbm_gbs": pk["hbm_gbs"], "peak_kind": pk_kind, "results": results}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill(args, dev):
     """one layer (288 routed + 1 shared) at prefill, T tokens (4096) of bf16 activations ~ N(0,1), expert
     popularity Zipf(1.1) over a seeded permutation, top-8. EXACT mode through the tensor-core GEMM path. Metric:
@@ -445,8 +523,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")
     ap.add_argument("--profile", action="store_true", help="device steps only (no e2e, sweep or CPU baseline): for ncu")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: configs[1] (the headline); prefill: configs[2] (4096 tokens, Zipf routing, TFLOP/s)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "sweep"],
+                    help="decode: configs[1] (the headline); prefill: configs[2] (4096 tokens, Zipf routing, TFLOP/s); "
+                         "sweep: configs[4] (bitrates x skews x batch sizes)")
     ap.add_argument("--tokens", type=int, default=4096, help="prefill tokens")
     ap.add_argument("--mode", type=int, default=2, choices=[1, 2], help="1 EXACT (fp16 weights, fp32 tensor-core sums), "
                     "2 I16 (int16 activations, exact integer tensor-core sums; bit-identical to the reference's I16 mode)")
@@ -476,10 +555,10 @@ def main():
     from glmx import MoELayer
     from glmx import _lib
 
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "sweep"):
         if world > 1:
-            raise SystemExit("the prefill workload runs on one GPU")
-        return run_prefill(args, dev)
+            raise SystemExit(f"the {args.workload} workload runs on one GPU")
+        return run_prefill(args, dev) if args.workload == "prefill" else run_sweep(args, dev)
     if world > 1:
         return run_expert_parallel(args, rank, world, dev, dist)
 

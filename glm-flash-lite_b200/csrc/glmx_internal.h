@@ -87,7 +87,7 @@ constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token 
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
 constexpr int I16_MAX_ROWS = 8192;     // I16 is the decode mode: its activation layout is sized for up to this many rows
 constexpr int PF_MAXM = 128;           // rows per job of the prefill GEMM (one tensor-core tile)
-constexpr int PF_AUTO_ROWS_PER_EXPERT = 32;   // EXACT mode takes the GEMM path from this many rows per expert on average
+constexpr int PF_AUTO_ROWS_PER_EXPERT = 12;   // EXACT mode takes the GEMM path from this many rows per expert on average
 constexpr int PF_KSPLIT = 3;           // K splits of the prefill gate/up GEMM (partial sums added in order in fp32)
 
 }  // namespace glmx

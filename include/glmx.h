@@ -45,7 +45,7 @@ extern "C" {
                                mode: at most 8192 rows (picks + shared-expert rows) per call */
 /* Path selection, OR'ed into the mode (EXACT only; default: chosen from the batch): GEMV = the decode kernels (one pass
  * over each expert's trellis per job of <= 8 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
- * <= 128 rows, trellis decoded into shared memory once per 128-row tile), the default once the call has >= 32 rows per
+ * <= 128 rows, trellis decoded into shared memory once per 128-row tile), the default once the call has >= 12 rows per
  * expert on average. The reference's large-batch schedule is moe_forward_band (ft_core.h:1617-1651). */
 #define GLMX_PATH_GEMV 0x100
 #define GLMX_PATH_GEMM 0x200

@@ -79,7 +79,7 @@ def test_prefill_baseline_geometry(oracle, dev):
 
 
 def test_prefill_auto_path_and_accumulate(oracle, dev):
-    """Above 32 rows per expert EXACT mode picks the GEMM path by itself; accumulate adds into fp16 out."""
+    """From 12 rows per expert EXACT mode picks the GEMM path by itself; accumulate adds into fp16 out."""
     from glmx import MoELayer, _lib, synth
     H, I, E, ntok, topk = 512, 256, 2, 80, 2
     bank = synth.make_bank(H, I, E, shared=True, seed=921)
