@@ -395,7 +395,8 @@ def run_expert_parallel(args, rank, world, dev, dist):
     """N > 1: configs[3]'s sharding on one layer. The 288 routed experts are split contiguously over the ranks
     (288/N each), the shared expert is replicated; the global decode batch (args.batch, 64) is split over the ranks
     (64/N tokens each, the tokens a data-parallel attention stage would own). A step = one expert-parallel layer
-    call (all-gather dispatch, local shard over all tokens, reduce-scatter return, shared expert overlapped).
+    call (all-gather dispatch, local shard + the shared expert on the own rows in one layer call, reduce-scatter
+    return).
     Strong scaling: the total work per step is the N=1 workload. Device time, max over ranks."""
     import torch
     from glmx import MoELayer, ep
@@ -419,11 +420,9 @@ def run_expert_parallel(args, rank, world, dev, dist):
                for m in (I, I, H)]
         return tr, ptrs, suh, svh
 
-    tr, ptrs, suh, svh = bank_of(n)
-    local = MoELayer(H, I, n, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev, first_expert=first)
-    tr_s, ptrs_s, suh_s, svh_s = bank_of(1)
-    shared = MoELayer(H, I, 1, ptrs_s, suh_s, svh_s, has_shared=False, keep=[tr_s], device=dev)
-    layer = ep.ExpertParallelLayer(local, shared, E=E)
+    tr, ptrs, suh, svh = bank_of(n + 1)          # the shard's n experts + the shared expert (local id n)
+    local = MoELayer(H, I, n + 1, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev)
+    layer = ep.ExpertParallelLayer(local, first, n, has_shared=True, E=E)
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
 
@@ -503,8 +502,8 @@ def run_expert_parallel(args, rank, world, dev, dist):
         "cpu_baseline": None,
         "e2e": {"value": Bg * args.steps / (E_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": world * (b * H * 2 + b * TOPK * 8),
                 "d2h_bytes_per_step": world * b * H * 4},
-        # per step and rank: split + transform + gate/up + epilogue + down + combine, for the shard and the shared expert
-        "gpu_launches": (12 if args.mode == 2 else 10) * args.steps * world,
+        # per step and rank: split + transform + gate/up + epilogue + down + combine (the shared expert rides along)
+        "gpu_launches": (6 if args.mode == 2 else 5) * args.steps * world,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

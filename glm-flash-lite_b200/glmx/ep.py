@@ -1,15 +1,15 @@
 """Expert parallelism: the routed experts of one MoE layer sharded over the ranks of a process group.
 
-Rank r of N holds routed experts [r*E/N, (r+1)*E/N) (a `MoELayer` with `first_expert = r*E/N`) and a copy of the
-shared expert; every rank owns B tokens (the data-parallel part of the model gives each rank its own tokens). Per
-layer call:
+Rank r of N holds routed experts [r*E/N, (r+1)*E/N) and a copy of the shared expert, in ONE `MoELayer` of n + 1
+experts (the shard at local ids 0..n-1, the shared expert at local id n); every rank owns B tokens (the data-parallel
+part of the model gives each rank its own tokens). Per layer call:
 
   dispatch   all-gather of the ranks' token rows x [B, H] and their routing (sel, w) [B, k] -> [N*B, ...]
-  compute    the local shard over all N*B tokens: its picks only (other shards' ids are skipped by the split),
-             weighted and summed per token into a partial [N*B, H] fp32 (tokens with no local pick get 0)
-  return     reduce-scatter (sum) of the partials -> out [B, H] fp32 for this rank's own tokens
-  shared     the shared expert over the rank's own B tokens, on a side stream while the dispatch is in flight,
-             written into the rank's own rows of the partial before the local shard accumulates into it
+  split      global ids -> local ids of this shard (others' ids masked to -1), plus one extra pick per row: the
+             shared expert (local id n, weight 1) for the rank's own B rows, masked for the other ranks' rows
+  compute    one layer call over all N*B rows: its picks only, weighted and summed per row into a partial [N*B, H]
+             fp32 (rows with no local pick get 0); the shared expert rides in the same launches as a routed expert
+  return     reduce-scatter (sum) of the partials -> out [B, H] fp32 for this rank's own rows
 
 With top-8 of 288 experts a token touches ≈ 5.3 of 8 shards, so gathering every token to every rank moves about as
 many bytes as a per-destination all-to-all, with static sizes: no host synchronisation for split sizes, and the
@@ -50,20 +50,20 @@ def _reduce_scatter(out: torch.Tensor, inp: torch.Tensor, group) -> None:
 class ExpertParallelLayer:
     """One MoE layer's routed experts sharded over `group` (see the module docstring).
 
-    local: the rank's shard, an object with `forward(x, sel, w, mode=, out=, accumulate=)` over global expert ids
-        (a `MoELayer` with `first_expert` set and no shared expert).
-    shared: the shared expert as a one-expert layer (`MoELayer(E=1)`), or None.
+    local: the rank's layer, an object with `forward(x, sel, w, mode=, out=, accumulate=)` over LOCAL expert ids
+        0..n-1 (the shard's experts first .. first + n - 1) and, when `has_shared`, local id n = the shared expert
+        (a `MoELayer` with n + 1 experts, `has_shared=False`).
+    first, n: the shard's expert range. E: routed experts of the whole layer.
     """
 
-    def __init__(self, local, shared=None, group=None, E: int | None = None):
+    def __init__(self, local, first: int, n: int, has_shared: bool = True, group=None, E: int | None = None):
         self.local = local
-        self.shared = shared
+        self.first, self.n, self.has_shared = int(first), int(n), bool(has_shared)
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.E = E
         self.device = getattr(local, "device", torch.device("cpu"))
-        self._side = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self._bufs = {}
 
     def _buf(self, name, shape, dtype):
@@ -73,30 +73,25 @@ class ExpertParallelLayer:
             self._bufs[name] = b
         return b
 
+    def _extra(self, NB: int, B: int):
+        """the shared-expert pick column: local id n with weight 1 on this rank's own rows, -1 / 0 elsewhere"""
+        key = ("extra", NB, B)
+        if key not in self._bufs:
+            own = torch.zeros(NB, dtype=torch.bool, device=self.device)
+            own[self.rank * B:(self.rank + 1) * B] = True
+            s = torch.where(own, self.n, -1).to(torch.int32).reshape(NB, 1)
+            self._bufs[key] = (s.contiguous(), own.to(torch.float32).reshape(NB, 1).contiguous())
+        return self._bufs[key]
+
     def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = 2,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """x [B, H] (same B on every rank), sel [B, k] global expert ids (< 0 = masked), w [B, k] -> out [B, H] fp32."""
         B, H = x.shape
         k = sel.shape[1]
-        N, r = self.world, self.rank
+        N = self.world
         x = x.contiguous()
         sel = sel.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()
-        partial = self._buf("partial", (N * B, H), torch.float32)
-        main = torch.cuda.current_stream(self.device) if self._side is not None else None
-
-        # shared expert over the own tokens, overlapping the dispatch
-        if self._side is not None:
-            self._side.wait_stream(main)
-            ctx = torch.cuda.stream(self._side)
-        else:
-            ctx = _null()
-        with ctx:
-            partial.zero_()
-            if self.shared is not None:
-                ones_s = self._buf("sh_sel", (B, 1), torch.int32).zero_()
-                ones_w = self._buf("sh_w", (B, 1), torch.float32).fill_(1.0)
-                self.shared.forward(x, ones_s, ones_w, mode=mode, out=partial[r * B:(r + 1) * B], accumulate=False)
 
         # dispatch: token rows and routing of every rank
         xg = self._buf("xg", (N * B, H), x.dtype)
@@ -104,27 +99,27 @@ class ExpertParallelLayer:
         route = torch.cat([sel, w.view(torch.int32)], dim=1)
         rg = self._buf("rg", (N * B, 2 * k), torch.int32)
         _all_gather(rg, route, self.group)
-        selg = rg[:, :k].contiguous()
-        wg = rg[:, k:].contiguous().view(torch.float32)
 
-        # compute: this shard's picks of all tokens, accumulated onto the shared rows
-        if self._side is not None:
-            main.wait_stream(self._side)
-        self.local.forward(xg, selg, wg, mode=mode, out=partial, accumulate=True)
+        # split: this shard's local ids (+ the shared expert on the own rows)
+        loc = rg[:, :k] - self.first
+        loc = torch.where((loc >= 0) & (loc < self.n), loc, torch.full_like(loc, -1))
+        wl = rg[:, k:].view(torch.float32)
+        if self.has_shared:
+            es, ew = self._extra(N * B, B)
+            loc = torch.cat([loc, es], dim=1)
+            wl = torch.cat([wl, ew], dim=1)
+        loc = loc.contiguous()
+        wl = wl.contiguous()
+
+        # compute: this shard's picks of all rows (+ shared on the own rows), one layer call
+        partial = self._buf("partial", (N * B, H), torch.float32)
+        self.local.forward(xg, loc, wl, mode=mode, out=partial, accumulate=False)
 
         # return: sum of the shards' partials, own rows
         if out is None:
             out = torch.empty((B, H), dtype=torch.float32, device=self.device)
         _reduce_scatter(out, partial, self.group)
         return out
-
-
-class _null:
-    def __enter__(self):
-        return self
-
-    def __exit__(self, *a):
-        return False
 
 
 def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0) -> ExpertParallelLayer:
@@ -148,12 +143,8 @@ def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0) -> Expert
         svh = [torch.from_numpy(np.ascontiguousarray(s[experts])).to(dev) for s in bank.svh]
         return tr, ptrs, suh, svh
 
-    tr, ptrs, suh, svh = upload(list(range(first, first + n)))
-    local = MoELayer(bank.H, bank.I, n, ptrs, suh, svh, bits=bank.bits, has_shared=False, act_limit=act_limit,
-                     keep=[tr], device=dev, first_expert=first)
-    shared = None
-    if bank.shared:
-        tr_s, ptrs_s, suh_s, svh_s = upload([bank.E])
-        shared = MoELayer(bank.H, bank.I, 1, ptrs_s, suh_s, svh_s, bits=bank.bits, has_shared=False,
-                          act_limit=act_limit, keep=[tr_s], device=dev)
-    return ExpertParallelLayer(local, shared, group, E=bank.E)
+    experts = list(range(first, first + n)) + ([bank.E] if bank.shared else [])
+    tr, ptrs, suh, svh = upload(experts)
+    local = MoELayer(bank.H, bank.I, len(experts), ptrs, suh, svh, bits=bank.bits, has_shared=False, act_limit=act_limit,
+                     keep=[tr], device=dev)
+    return ExpertParallelLayer(local, first, n, has_shared=bank.shared, group=group, E=bank.E)

@@ -19,19 +19,19 @@ def f_expert(e, x):
 
 
 class FakeShard:
-    """forward(x, sel, w, out, accumulate) over global ids, keeping only ids in [first, first + n)."""
+    """A shard's layer over LOCAL ids: 0..n-1 are global experts first..first+n-1, id n is the shared expert."""
 
-    def __init__(self, first, n, const_expert=None):
-        self.first, self.n, self.const = first, n, const_expert
+    def __init__(self, first, n):
+        self.first, self.n = first, n
         self.device = torch.device("cpu")
 
     def forward(self, x, sel, w, mode=2, out=None, accumulate=False):
         y = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32)
         for t in range(x.shape[0]):
             for j in range(sel.shape[1]):
-                e = int(sel[t, j]) - self.first
-                if 0 <= e < self.n:
-                    y[t] += float(w[t, j]) * f_expert(self.const if self.const is not None else e + self.first, x[t].float())
+                e = int(sel[t, j])
+                if 0 <= e <= self.n:
+                    y[t] += float(w[t, j]) * f_expert(99 if e == self.n else e + self.first, x[t].float())
         if accumulate:
             out += y
         else:
@@ -63,7 +63,7 @@ def _worker(rank, world, port, B, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         first, n = ep.shard_range(E, world, rank)
-        layer = ep.ExpertParallelLayer(FakeShard(first, n), FakeShard(0, 1, const_expert=99), E=E)
+        layer = ep.ExpertParallelLayer(FakeShard(first, n), first, n, has_shared=True, E=E)
         x, sel, w = inputs(rank, B)
         out = layer.forward(x, sel, w)
         err = float((out - reference(x, sel, w)).abs().max())
