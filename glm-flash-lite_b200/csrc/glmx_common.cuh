@@ -64,16 +64,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
-// Bounded wait: returns false (and the caller records an error and leaves its loop) once WAIT_TIMEOUT_NS passed.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity)
+// Bounded wait: returns false (and the caller records an error and leaves its loop) once timeout_ns passed.
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint64_t* bar, uint32_t parity, uint64_t timeout_ns)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true)
     {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > (uint64_t) WAIT_TIMEOUT_NS) return false;
+        if (globaltimer() - t0 > timeout_ns) return false;
     }
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity)
+{
+    return mbar_wait_bounded_ns(bar, parity, (uint64_t) WAIT_TIMEOUT_NS);
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes and addresses 16-byte aligned)

@@ -37,7 +37,8 @@ class GlmxError(RuntimeError):
 # every symbol include/glmx.h declares
 EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_destroy", "glmx_layer_set_act_limit",
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
-           "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc")
+           "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc",
+           "glmx_selftest_bounded_wait")
 NOALLOC_SCRATCH_BYTES = 48 << 20
 
 _lib = None
@@ -77,6 +78,8 @@ def load(path: str = LIB_PATH):
     L.glmx_moe_forward_noalloc.restype = _I
     L.glmx_moe_forward_hc.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _I, _P, C.c_size_t, _P]
     L.glmx_moe_forward_hc.restype = _I
+    L.glmx_selftest_bounded_wait.argtypes = [_I, _P, _P]
+    L.glmx_selftest_bounded_wait.restype = _I
     if L.glmx_version() != ABI_VERSION:
         raise RuntimeError(f"libglmx ABI {L.glmx_version()} != {ABI_VERSION}")
     _lib = L

@@ -136,6 +136,12 @@ GLMX_API int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint1
  * sticky ctrl words and stats (kernels/cpu_avx2/ft_tier_cu.cu:33-52, 176-193). */
 GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* workspace, void* stream, int* flags);
 
+/* Failure-detection self-test (no counterpart in the reference, whose device waits also give up after a limit,
+ * kernels/cpu_avx2/ft_tier_cu.cu:176-193): launches one warp that runs the library's bounded mbarrier wait on a
+ * barrier nothing completes; after timeout_us (1 .. 1e7) it gives up and ORs the timeout bit into the device int
+ * *flag (the bit glmx_check reports for a stalled forward). The kernel returns normally; the context stays usable. */
+GLMX_API int glmx_selftest_bounded_wait(int timeout_us, int* flag, void* stream);
+
 /* Size of the scratch built into the library for glmx_moe_forward_noalloc: 48 MiB, which holds the workspace of up
  * to 8 tokens x top-8 (+ a shared expert) at H = 6144, I = 1536, in either mode. */
 #define GLMX_NOALLOC_SCRATCH_BYTES (48u << 20)

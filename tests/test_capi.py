@@ -38,3 +38,5 @@ def test_version_and_error_without_gpu():
     assert L.glmx_layer_create(C.byref(d), C.byref(h)) == _lib.E_ARG
     assert b"multiples of 128" in L.glmx_last_error()
     assert L.glmx_decode_tiles(None, 5, 1, None, None) == _lib.E_ARG
+    assert L.glmx_selftest_bounded_wait(0, None, None) == _lib.E_ARG
+    assert b"timeout_us" in L.glmx_last_error()
