@@ -260,6 +260,108 @@ def run_sweep(args, dev):
     print(json.dumps(line), flush=True)
 
 
+def decode_layer(dev, g, n_experts):
+    """configs[1]'s layer on the device: n_experts routed + 1 shared expert, K=3 trellis from uniform random bytes,
+    suh = +-1, svh = +-|N(0.02, 0.005)|."""
+    import torch
+    from glmx import MoELayer
+    et = n_experts + 1
+    bank = torch.randint(0, 256, (et * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
+    base = bank.data_ptr()
+    proj = (H // 16) * (I // 16) * 96
+    ptrs = torch.tensor([[base + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(et)], dtype=torch.int64)
+    sign = lambda shape: torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
+    suh = [sign((et, k)).half() for k in (H, H, I)]
+    svh = [(sign((et, n)) * (0.02 + 0.005 * torch.randn((et, n), device=dev, generator=g)).abs()).half() for n in (I, I, H)]
+    return MoELayer(H, I, n_experts, ptrs, suh, svh, bits=(3, 3, 3), has_shared=True, keep=[bank], device=dev)
+
+
+def run_router(args, dev):
+    """Router in front of the split (glmx_router): gate linear (bf16 W [288, 6144], bf16 z), sigmoid + bias, top-8,
+    renormalised weights, at the decode batch and the prefill size. Device time per call with CUDA events on the
+    launching stream; L2 flushed (1 GiB write, longer than the host's launch overhead so the GPU never waits for the
+    launch inside the events) before every call, outside the timed events: the gate matrix is 3.5 MB and would
+    otherwise be read from L2. `warm_ms`: back-to-back calls, L2-resident gate matrix."""
+    import torch
+    from glmx import Router
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    W = (0.02 * torch.randn((E, H), device=dev, generator=g)).to(torch.bfloat16)
+    bias = 0.1 * torch.randn((E,), device=dev, generator=g)
+    r = Router(W, bias, TOPK, 1, 1, True, 1.0)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    pk, pk_kind = peaks()
+    out = {}
+    for ntok in (args.batch, args.tokens):
+        z = torch.randn((ntok, H), device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(args.warmup):
+            r(z)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        torch.cuda.synchronize(dev)
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            r(z)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        for _ in range(args.steps):
+            r(z)
+        w1.record(stream)
+        torch.cuda.synchronize(dev)
+        warm_ms = w0.elapsed_time(w1) / args.steps
+        byts = E * H * 2 + ntok * H * 2 + ntok * E * 4 + ntok * TOPK * 8
+        out[ntok] = {"ms": ms, "warm_ms": warm_ms, "tok_per_s": ntok / (ms / 1e3), "algorithmic_bytes": byts,
+                     "gbs": byts / (ms / 1e3) / 1e9,
+                     "tflops": 2.0 * ntok * E * H / (ms / 1e3) / 1e12}
+    # in context: a decode step = router (fp16 activations, the layer's input) + the layer on its picks, back to back,
+    # against the layer alone on precomputed picks of the same batch
+    from glmx import _lib
+    layer = decode_layer(dev, g, E)
+    in_context = {}
+    for B in sorted({1, 8, args.batch}):
+        z = torch.randn((B, H), device=dev, generator=g).half()
+        sel0, w0, _ = r(z)
+        outb = torch.empty((B, H), dtype=torch.float32, device=dev)
+
+        def both():
+            sel, w, _ = r(z)
+            layer.forward(z, sel, w, out=outb, mode=_lib.MODE_I16)
+
+        def alone():
+            layer.forward(z, sel0, w0, out=outb, mode=_lib.MODE_I16)
+
+        res = {}
+        for name, fn in (("layer_ms", alone), ("router_and_layer_ms", both)):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            res[name] = e0.elapsed_time(e1) / args.steps
+        res["router_share"] = 1.0 - res["layer_ms"] / res["router_and_layer_ms"]
+        in_context[str(B)] = res
+    del layer
+    head = out[args.batch]
+    line = {"metric": "router_tok_per_s", "value": head["tok_per_s"], "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 in, fp32 logits", "data": "synthetic",
+            "config": {"workload": f"router of one configs[1] layer: B={args.batch} tokens, 288 experts, H=6144, top-8, "
+                                   "bias, renormalised", "l2": "flushed before every call"},
+            "roofline": {"bound": "hbm", "kernel": "router_gate_kernel", "achieved": head["gbs"], "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": head["gbs"] / pk["hbm_gbs"], "peak_kind": pk_kind, "traffic": None},
+            "gpu_launches": args.steps, "sizes": {str(k): v for k, v in out.items()}, "in_context": in_context}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill(args, dev):
     """one layer (288 routed + 1 shared) at prefill, T tokens (4096) of bf16 activations ~ N(0,1), expert
     popularity Zipf(1.1) over a seeded permutation, top-8. EXACT mode through the tensor-core GEMM path. Metric:
@@ -522,7 +624,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")
     ap.add_argument("--profile", action="store_true", help="device steps only (no e2e, sweep or CPU baseline): for ncu")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "sweep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "sweep", "router"],
                     help="decode: configs[1] (the headline); prefill: configs[2] (4096 tokens, Zipf routing, TFLOP/s); "
                          "sweep: configs[4] (bitrates x skews x batch sizes)")
     ap.add_argument("--tokens", type=int, default=4096, help="prefill tokens")
@@ -554,26 +656,18 @@ def main():
     from glmx import MoELayer
     from glmx import _lib
 
-    if args.workload in ("prefill", "sweep"):
+    if args.workload in ("prefill", "sweep", "router"):
         if world > 1:
             raise SystemExit(f"the {args.workload} workload runs on one GPU")
-        return run_prefill(args, dev) if args.workload == "prefill" else run_sweep(args, dev)
+        return {"prefill": run_prefill, "sweep": run_sweep, "router": run_router}[args.workload](args, dev)
     if world > 1:
         return run_expert_parallel(args, rank, world, dev, dist)
 
     # ---- synthetic layer on the device: 289 experts x (gate|up|down) K=3 trellis + scales ----
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
-    et = E + 1
-    bank = torch.randint(0, 256, (et * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
-    base = bank.data_ptr()
+    layer = decode_layer(dev, g, E)
     proj = (H // 16) * (I // 16) * 96
-    ptrs = torch.tensor([[base + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(et)], dtype=torch.int64)
-    def sign(shape):
-        return torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
-    suh = [sign((et, k)).half() for k in (H, H, I)]
-    svh = [(sign((et, n)) * (0.02 + 0.005 * torch.randn((et, n), device=dev, generator=g)).abs()).half() for n in (I, I, H)]
-    layer = MoELayer(H, I, E, ptrs, suh, svh, bits=(3, 3, 3), has_shared=True, keep=[bank], device=dev)
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
 

@@ -38,8 +38,9 @@ class GlmxError(RuntimeError):
 EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_destroy", "glmx_layer_set_act_limit",
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
            "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc",
-           "glmx_selftest_bounded_wait")
+           "glmx_selftest_bounded_wait", "glmx_router")
 NOALLOC_SCRATCH_BYTES = 48 << 20
+ROUTER_MAX_EXPERTS = 512
 
 _lib = None
 
@@ -80,6 +81,8 @@ def load(path: str = LIB_PATH):
     L.glmx_moe_forward_hc.restype = _I
     L.glmx_selftest_bounded_wait.argtypes = [_I, _P, _P]
     L.glmx_selftest_bounded_wait.restype = _I
+    L.glmx_router.argtypes = [_P, _I, _I, _I, _P, _I, _P, _I, _I, _I, _I, _I, C.c_float, _P, _P, _I, _P, _I, _P]
+    L.glmx_router.restype = _I
     if L.glmx_version() != ABI_VERSION:
         raise RuntimeError(f"libglmx ABI {L.glmx_version()} != {ABI_VERSION}")
     _lib = L

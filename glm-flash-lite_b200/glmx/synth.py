@@ -158,3 +158,13 @@ def route_hotset(ntok: int, E: int, topk: int, hot: int, frac: float, seed: int)
 def unique_experts(sel: np.ndarray, E: int) -> int:
     s = sel[(sel >= 0) & (sel < E)]
     return int(np.unique(s).size)
+
+
+def router_inputs(ntok: int, E: int, seed: int, logit_scale: float = 6.0, bias_scale: float = 0.5):
+    """Router test inputs from the SplitMix64 stream of `seed` (no RNG library involved, so every machine makes the
+    same values): fp32 logits uniform in +-logit_scale/2 at 24-bit resolution [ntok, E] and a score-correction bias
+    uniform in +-bias_scale/2 [E]."""
+    u = (splitmix_u64(seed, ntok * E + E) >> np.uint64(40)).astype(np.float64) / float(1 << 24)
+    logits = (logit_scale * (u[: ntok * E] - 0.5)).astype(np.float32).reshape(ntok, E)
+    bias = (bias_scale * (u[ntok * E:] - 0.5)).astype(np.float32)
+    return logits, bias

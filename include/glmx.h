@@ -142,6 +142,21 @@ GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* works
  * *flag (the bit glmx_check reports for a stalled forward). The kernel returns normally; the context stays usable. */
 GLMX_API int glmx_selftest_bounded_wait(int timeout_us, int* flag, void* stream);
 
+/* Router of the MoE site, in front of the split: the GLM-4 MoE routing that exllamav3's router produces for the
+ * reference's routing_fn hook (glm53/cpu_tier.py:305-335, sel [bsz, k] and w [bsz, k]). With gate_w (E x hidden,
+ * row-major, dtype gate_dtype) the logits are computed first, logits[t][e] = sum_h z[t][h] * gate_w[e][h] with exact
+ * products and fp32 sums (z: [ntok][hidden], dtype z_dtype; hidden a multiple of 32; both pointers 16-byte aligned),
+ * and written to `logits`; with gate_w == NULL, `logits` (fp32 [ntok][n_experts]) is the input. Then per token:
+ * s = sigmoid(logit), c = s + bias (bias fp32 [n_experts] or NULL); with n_group > 1 the topk_group groups of largest
+ * (top-2 sum of c) stay and c is 0 elsewhere; picks = the topk largest c, in descending order, equal values by smaller
+ * id; w = s[pick], if norm w / (sum of the picks' s + 1e-20), then * scale. sel: [ntok][topk] GLMX_I32 or GLMX_I64;
+ * w: [ntok][topk] float dtype w_dtype. Limits: n_experts <= GLMX_ROUTER_MAX_EXPERTS, n_group <= 32 dividing n_experts,
+ * topk <= 32. Two kernels on `stream`, nothing allocated. */
+#define GLMX_ROUTER_MAX_EXPERTS 512
+GLMX_API int glmx_router(const void* z, int z_dtype, int ntok, int hidden, const void* gate_w, int gate_dtype,
+                         const float* bias, int n_experts, int n_group, int topk_group, int topk, int norm, float scale,
+                         float* logits, void* sel, int sel_dtype, void* w, int w_dtype, void* stream);
+
 /* Size of the scratch built into the library for glmx_moe_forward_noalloc: 48 MiB, which holds the workspace of up
  * to 8 tokens x top-8 (+ a shared expert) at H = 6144, I = 1536, in either mode. */
 #define GLMX_NOALLOC_SCRATCH_BYTES (48u << 20)

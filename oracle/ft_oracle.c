@@ -372,3 +372,121 @@ void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, con
             }
         }
 }
+
+/* ---- router in front of the split (the GLM-4 MoE routing of exllamav3's router, as transformers states it in
+ * models/glm4_moe/modeling_glm4_moe.py:302-305 (gate) and 389-412 (route_tokens_to_experts)) ---- */
+
+/* 2^k as an fp32 (k in [-149, 127]; below that 0) */
+static float pow2i_f(int k)
+{
+    uint32_t b;
+    float f;
+    if (k >= -126) b = (uint32_t) (k + 127) << 23;
+    else if (k >= -149) b = 1u << (k + 149);
+    else return 0.0f;
+    memcpy(&f, &b, sizeof f);
+    return f;
+}
+
+/* e^y in fp32: Cody and Waite's argument reduction (y = n ln2 + r, ln2 split into a 16-bit head and a tail) and the
+ * degree-8 Taylor polynomial of e^r in Horner form with fused multiply-adds, 2^n applied in two halves. The same fp32
+ * operation sequence as the GPU router's, so both give the same bits. */
+static float exp_cw(float y)
+{
+    if (y != y) return y;
+    y = fminf(fmaxf(y, -175.0f), 175.0f);
+    const float n = rintf(y * 1.44269502162933349609375f);
+    float r = fmaf(n, -0.693145751953125f, y);
+    r = fmaf(n, -1.428606765330187045037746429443359375e-06f, r);
+    float p = 2.4801587301587302e-05f;
+    p = fmaf(p, r, 1.9841269841269841e-04f);
+    p = fmaf(p, r, 1.3888888888888889e-03f);
+    p = fmaf(p, r, 8.3333333333333332e-03f);
+    p = fmaf(p, r, 4.1666666666666664e-02f);
+    p = fmaf(p, r, 1.6666666666666666e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int) n, n1 = ni / 2, n2 = ni - n1;
+    return (p * pow2i_f(n1)) * pow2i_f(n2);
+}
+
+static float router_sigmoid(float x) { return 1.0f / (1.0f + exp_cw(-x)); }
+
+void fto_router_sigmoid(const float* x, int n, float* out)
+{
+    for (int i = 0; i < n; ++i) out[i] = router_sigmoid(x[i]);
+}
+
+/* (v, i) before (u, j): larger value first, equal values by smaller index */
+static int router_better(float v, int i, float u, int j) { return v > u || (v == u && i < j); }
+
+void fto_router_gate(const float* z, int ntok, int H, const float* W, int E, float* logits)
+{
+    for (int t = 0; t < ntok; ++t)
+        for (int e = 0; e < E; ++e)
+        {
+            double s = 0.0;
+            for (int h = 0; h < H; ++h) s += (double) z[(size_t) t * H + h] * (double) W[(size_t) e * H + h];
+            logits[(size_t) t * E + e] = (float) s;
+        }
+}
+
+void fto_router_select(const float* logits, int ntok, int E, const float* bias, int n_group, int topk_group, int topk,
+                       int norm, float scale, int32_t* sel, float* w)
+{
+    float* s = (float*) malloc(sizeof(float) * (size_t) E);
+    float* c = (float*) malloc(sizeof(float) * (size_t) E);
+    unsigned char* taken = (unsigned char*) malloc((size_t) E);
+    const int G = E / n_group;
+    for (int t = 0; t < ntok; ++t)
+    {
+        for (int e = 0; e < E; ++e)
+        {
+            s[e] = router_sigmoid(logits[(size_t) t * E + e]);
+            c[e] = bias ? s[e] + bias[e] : s[e];
+            taken[e] = 0;
+        }
+        if (n_group > 1)
+        {
+            float gs[64];
+            for (int g = 0; g < n_group; ++g)
+            {
+                float m1 = -INFINITY, m2 = -INFINITY;
+                for (int e = g * G; e < (g + 1) * G; ++e)
+                {
+                    if (c[e] > m1) { m2 = m1; m1 = c[e]; }
+                    else if (c[e] > m2) m2 = c[e];
+                }
+                gs[g] = m1 + m2;
+            }
+            for (int g = 0; g < n_group; ++g)
+            {
+                int rank = 0;
+                for (int h = 0; h < n_group; ++h) rank += router_better(gs[h], h, gs[g], g);
+                if (rank >= topk_group)
+                    for (int e = g * G; e < (g + 1) * G; ++e) c[e] = 0.0f;
+            }
+        }
+        float wsum = 0.0f;
+        for (int r = 0; r < topk; ++r)
+        {
+            int bi = -1;
+            for (int e = 0; e < E; ++e)
+                if (!taken[e] && (bi < 0 || router_better(c[e], e, c[bi], bi))) bi = e;
+            taken[bi] = 1;
+            sel[(size_t) t * topk + r] = bi;
+            w[(size_t) t * topk + r] = s[bi];
+            wsum += s[bi];
+        }
+        for (int r = 0; r < topk; ++r)
+        {
+            float v = w[(size_t) t * topk + r];
+            if (norm) v = v / (wsum + 1e-20f);
+            w[(size_t) t * topk + r] = v * scale;
+        }
+    }
+    free(s);
+    free(c);
+    free(taken);
+}

@@ -91,6 +91,19 @@ void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* sha
  * post [R][4], comb [R][4][4] (comb[h][g]): x_g <- fma(comb[3][g], x_3, ... fma(comb[0][g], x_0, post_g * y)). */
 void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, const float* comb);
 
+/* Router in front of the split: the GLM-4 MoE routing of exllamav3's router (un-vendored third-party code), as the
+ * published model code states it (transformers, models/glm4_moe/modeling_glm4_moe.py:302-305 and 389-412).
+ * fto_router_gate: logits[t][e] = sum_h z[t][h] * W[e][h], accumulated in fp64 and rounded once (the reference
+ * accumulates in fp32 in an order of its own; this is the exact value it approximates).
+ * fto_router_select: s = sigmoid(logit) = 1 / (1 + e^-logit) with e^y from a fixed fp32 sequence (Cody-Waite reduction,
+ * degree-8 Taylor polynomial; fto_router_sigmoid exposes it), c = s + bias; n_group > 1: group score = sum of
+ * the two largest c of each group, c = 0 outside the topk_group best groups; picks = topk largest c in descending
+ * order (equal values: smaller id first); w = s[pick], norm: w / (sum in pick order + 1e-20), then * scale. */
+void fto_router_gate(const float* z, int ntok, int H, const float* W, int E, float* logits);
+void fto_router_sigmoid(const float* x, int n, float* out);
+void fto_router_select(const float* logits, int ntok, int E, const float* bias, int n_group, int topk_group, int topk,
+                       int norm, float scale, int32_t* sel, float* w);
+
 #ifdef __cplusplus
 }
 #endif

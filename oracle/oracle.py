@@ -66,6 +66,9 @@ class Oracle:
         L.fto_moe_forward.argtypes = [_P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P, _I, _P]
         L.fto_expert_i16.argtypes = [_P, _I, _I, _F, _P, _I, _P]
         L.fto_hc_apply.argtypes = [_P, _P, _I, _I, _P, _P]
+        L.fto_router_gate.argtypes = [_P, _I, _I, _P, _I, _P]
+        L.fto_router_sigmoid.argtypes = [_P, _I, _P]
+        L.fto_router_select.argtypes = [_P, _I, _I, _P, _I, _I, _I, _I, _F, _P, _P]
         L.fto_init()
         self.L = L
 
@@ -94,6 +97,33 @@ class Oracle:
         self.L.fto_hc_apply(_ptr(x), _ptr(np.ascontiguousarray(y, np.float32)), R, D,
                             _ptr(np.ascontiguousarray(post, np.float32)), _ptr(np.ascontiguousarray(comb, np.float32)))
         return x
+
+    # --- router ----------------------------------------------------------------------------------------------
+    def router_gate(self, z: np.ndarray, W: np.ndarray) -> np.ndarray:
+        """logits [ntok, E] = z [ntok, H] . W [E, H]^T, fp64 accumulation rounded once (fto_router_gate)."""
+        z = np.ascontiguousarray(z, np.float32)
+        W = np.ascontiguousarray(W, np.float32)
+        out = np.empty((z.shape[0], W.shape[0]), np.float32)
+        self.L.fto_router_gate(_ptr(z), z.shape[0], z.shape[1], _ptr(W), W.shape[0], _ptr(out))
+        return out
+
+    def router_sigmoid(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.L.fto_router_sigmoid(_ptr(x), x.size, _ptr(out))
+        return out
+
+    def router_select(self, logits: np.ndarray, bias=None, topk: int = 8, n_group: int = 1, topk_group: int = 1,
+                      norm: bool = True, scale: float = 1.0):
+        """(sel int32 [ntok, topk], w fp32 [ntok, topk]) from fp32 logits (fto_router_select)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        ntok, E = logits.shape
+        sel = np.empty((ntok, topk), np.int32)
+        w = np.empty((ntok, topk), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self.L.fto_router_select(_ptr(logits), ntok, E, None if b is None else _ptr(b), n_group, topk_group, topk,
+                                 int(bool(norm)), float(scale), _ptr(sel), _ptr(w))
+        return sel, w
 
     def prep_block(self, x: np.ndarray, suh: np.ndarray) -> np.ndarray:
         xt = np.empty(128, np.float32)

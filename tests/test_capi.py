@@ -40,3 +40,10 @@ def test_version_and_error_without_gpu():
     assert L.glmx_decode_tiles(None, 5, 1, None, None) == _lib.E_ARG
     assert L.glmx_selftest_bounded_wait(0, None, None) == _lib.E_ARG
     assert b"timeout_us" in L.glmx_last_error()
+    R = lambda E, ng, tg, k, ntok=4: L.glmx_router(None, _lib.F32, ntok, 0, None, _lib.F32, None, E, ng, tg, k, 1, 1.0,
+                                                   None, None, _lib.I32, None, _lib.F32, None)
+    assert R(513, 1, 1, 8) == _lib.E_ARG                  # more experts than the selection scratch holds
+    assert R(288, 5, 1, 8) == _lib.E_ARG                  # groups must divide the experts
+    assert R(288, 8, 2, 80) == _lib.E_ARG                 # topk beyond the kept groups
+    assert R(288, 1, 1, 8) == _lib.E_ARG and b"required" in L.glmx_last_error()   # null outputs
+    assert R(288, 1, 1, 8, ntok=-1) == _lib.E_ARG

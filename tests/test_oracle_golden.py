@@ -1,9 +1,12 @@
 """Pins the CPU restatement (oracle/ft_oracle.c) against fixtures produced by the reference's own ft_core.h
-(tests/golden/make_golden.py). CPU only."""
+(tests/golden/make_golden.py), and the router restatement against the published GLM-4 MoE routing
+(tests/golden/make_router_golden.py). CPU only."""
+import sys
+
 import numpy as np
 import pytest
 
-from conftest import golden_bank, load_golden, parity
+from conftest import GOLDEN, golden_bank, load_golden, parity
 
 
 def test_decode_known_answers(oracle):
@@ -100,3 +103,64 @@ def test_hc_apply_restatement(oracle):
         np.einsum("rhg,rhd->rgd", comb.astype(np.float64), x.astype(np.float64))
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
     np.testing.assert_array_equal(x, oracle.hc_apply(x, y, post, comb) * 0 + x)      # input untouched
+
+
+def _router_case(name):
+    sys.path.insert(0, GOLDEN)
+    import make_router_golden as M
+    return M
+
+
+def test_router_restatement_vs_published_routing(oracle):
+    """The router restatement (fto_router_select / fto_router_gate) against the GLM-4 MoE routing as transformers runs
+    it (tests/golden/make_router_golden.py): the same experts for every token, weights within 8 fp32 ulps (the
+    published code sums the 8 weights in an order of its own and uses fp32 sigmoid)."""
+    from glmx import synth
+    M = _router_case("router")
+    d = load_golden("router")
+    for name, (ntok, E, topk, ng, tg, norm, scale, wb, seed) in M.CASES.items():
+        logits, bias = synth.router_inputs(ntok, E, seed)
+        sel, w = oracle.router_select(logits, bias if wb else None, topk, ng, tg, norm, scale)
+        order = np.argsort(sel, axis=1, kind="stable")
+        np.testing.assert_array_equal(np.take_along_axis(sel, order, 1), d[name + "_sel"], err_msg=name)
+        np.testing.assert_allclose(np.take_along_axis(w, order, 1), d[name + "_w"], rtol=1e-6, atol=0, err_msg=name)
+        # picks in descending choice score (c = sigmoid + bias)
+        c = 1.0 / (1.0 + np.exp(-logits.astype(np.float64))) + (bias if wb else 0.0)
+        cs = np.take_along_axis(c, sel, 1)
+        assert (np.diff(cs, axis=1) <= 0).all(), name
+    z, W = M.gate_inputs(**M.GATE)
+    logits = oracle.router_gate(z, W)
+    np.testing.assert_allclose(logits, d["gate_logits"], rtol=0, atol=2e-5 * float(np.abs(d["gate_logits"]).max()))
+    sel, w = oracle.router_select(logits, None, 8, 1, 1, True, 1.0)
+    order = np.argsort(sel, axis=1, kind="stable")
+    np.testing.assert_array_equal(np.take_along_axis(sel, order, 1), d["gate_sel"])
+    np.testing.assert_allclose(np.take_along_axis(w, order, 1), d["gate_w"], rtol=1e-6, atol=0)
+
+
+def test_router_restatement_ties_and_groups(oracle):
+    """Equal scores go to the smaller expert id; experts outside the kept groups are never picked while a kept group
+    still has candidates."""
+    logits = np.zeros((2, 16), np.float32)
+    sel, w = oracle.router_select(logits, None, 4, 1, 1, True, 1.0)
+    np.testing.assert_array_equal(sel, [[0, 1, 2, 3]] * 2)
+    np.testing.assert_array_equal(w, np.full((2, 4), np.float32(0.25)))
+    logits = np.full((1, 16), -3.0, np.float32)
+    logits[0, [1, 9]] = 4.0                      # group 0 (ids 0..7) and group 1 (8..15): both have one big score
+    logits[0, 10] = 3.0                          # group 1 has the larger top-2 sum
+    sel, _ = oracle.router_select(logits, None, 3, 2, 1, False, 1.0)
+    assert set(sel[0].tolist()) <= set(range(8, 16)) and sel[0, 0] == 9 and sel[0, 1] == 10
+
+
+def test_router_sigmoid_error_bound(oracle):
+    """The router's fp32 sigmoid (own Cody-Waite exp, identical fp32 steps on the CPU and the GPU) stays within 2.5 ulp
+    of the exact value wherever the result is a normal fp32 number (x >= -87; below that, like torch's fp32 sigmoid,
+    it returns 0 once e^-x overflows), and is exact at the ends."""
+    x = np.concatenate([np.linspace(-87, 95, 400001, dtype=np.float32),
+                        np.random.default_rng(5).standard_normal(200000).astype(np.float32) * 4])
+    s = oracle.router_sigmoid(x).astype(np.float64)
+    t = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
+    ulp = np.spacing(t.astype(np.float32)).astype(np.float64)
+    assert (np.abs(s - t) / ulp).max() <= 2.5
+    ends = oracle.router_sigmoid(np.array([0.0, 100.0, -100.0, np.inf, -np.inf], np.float32))
+    np.testing.assert_array_equal(ends, np.array([0.5, 1.0, 0.0, 1.0, 0.0], np.float32))
+    assert np.isnan(oracle.router_sigmoid(np.array([np.nan], np.float32))[0])
