@@ -224,6 +224,25 @@ __device__ __forceinline__ void decode_frag_tc_from(uint32_t hi, uint32_t lo, co
     a[3] = codebook_pair(d2[2], d2[3]);
 }
 
+// Decoded fp16 weights of one tile as an m16n8k16 A fragment of the transposed tile (rows = output columns n, columns =
+// inputs k) in NATURAL input order: the trellis stream order is that fragment layout (ft_core.h:48-61 PERM: lane
+// (g, tq)'s stream weights 8*lane .. 8*lane+7 sit at (k, n) = (2tq, g), (2tq+1, g), (2tq+8, g), (2tq+9, g), then the
+// same k at n = g+8). Byte sums on the integer pipe (dp4a against 0x01010101, accumulated onto 0x6400 so each sum is
+// the fp16 pattern of 1024 + s), then the codebook FMA per pair.
+template <int K>
+__device__ __forceinline__ void decode_frag_nat(uint32_t hi, uint32_t lo, const LaneDecode<K>& L, uint32_t a[4])
+{
+    uint32_t x[8];
+    decode_words_from<K>(hi, lo, L, x);
+    uint32_t s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = (uint32_t) __dp4a(x[j], 0x01010101u, 0x6400u);
+    a[0] = codebook_pair(s[0], s[1]);     // n = g,     k = 2tq, 2tq+1
+    a[1] = codebook_pair(s[4], s[5]);     // n = g + 8, k = 2tq, 2tq+1
+    a[2] = codebook_pair(s[2], s[3]);     // n = g,     k = 2tq+8, 2tq+9
+    a[3] = codebook_pair(s[6], s[7]);     // n = g + 8, k = 2tq+8, 2tq+9
+}
+
 __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
 {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"

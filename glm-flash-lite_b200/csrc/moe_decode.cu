@@ -307,6 +307,7 @@ struct PrepArgs
     const __half* suh_g; const __half* suh_u;
     __half* xg; __half* xu;
     int rows_max;
+    int natural;          // 1: natural input order (tensor-core GEMM), 0: PERM16 order inside 16-row tiles (GEMV)
 };
 
 __device__ __forceinline__ float load_x(const void* x, int dt, size_t i)
@@ -338,8 +339,8 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
 #pragma unroll
     for (int q = 0; q < 4; ++q)
     {
-        const int c = lane + 32 * q;             // PERM16 order inside each 16-row tile (decode_frag_tc)
-        out[(c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
+        const int c = lane + 32 * q;             // GEMV: PERM16 order inside each 16-row tile (decode_frag_tc)
+        out[a.natural ? c : (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
     }
 }
 
@@ -537,7 +538,8 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     return w;
 }
 
-cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st)
+cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st,
+                              bool natural)
 {
     const int rows = lay.rows_max;
     if (rows <= 0) return cudaSuccess;
@@ -550,6 +552,7 @@ cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_
     p.xg = reinterpret_cast<__half*>(ws + lay.xg);
     p.xu = reinterpret_cast<__half*>(ws + lay.xu);
     p.rows_max = rows;
+    p.natural = natural ? 1 : 0;
     const long long warps = (long long) rows * 2 * (L.H / 128);
     prep_kernel<<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(p);
     return cudaGetLastError();

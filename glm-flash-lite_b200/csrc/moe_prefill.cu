@@ -2,11 +2,12 @@
 // 5th-generation tensor cores. Per (job of <= 128 rows of one expert, column block of TN = 256 (else 128) outputs,
 // projection, K split) tile:
 //
-//   A  = the rows' transformed activations (fp16, PERM16 order inside each 16-input group), [128 x 64] per stage,
+//   A  = the rows' transformed activations (fp16, natural input order), [128 x 64] per stage,
 //        loaded by the tensor-memory-access unit from the row-major activation buffer with the 128-byte swizzle
 //   B  = the expert's trellis tiles for the stage (4 k-rows x TN/16 tiles), bulk-copied to shared memory, decoded by
-//        8 warps into fp16 (tensor-core byte sums + codebook FMA, decode_frag_tc_from) and written with stmatrix into
-//        the K-major interleaved layout the MMA reads
+//        8 warps into fp16 (integer byte sums with dp4a + codebook FMA, decode_frag_nat: a lane's 8 stream weights are
+//        exactly its m16n8k16 fragment of the transposed tile) and written with stmatrix into the K-major interleaved
+//        layout the MMA reads. The byte sums stay off the tensor pipe, which the tcgen05 MMAs keep busy
 //   D  = fp32 accumulators in tensor memory (tcgen05.mma kind::f16, M=128, N=TN, K=16 per instruction). Long K sums
 //        are kept short: gate/up split K=6144 over 3 tiles (partial sums added in order in fp32 by the epilogue
 //        kernel), and inside a tile 128-input block b accumulates into chain b % (512 / TN) of tensor memory, the chains
@@ -14,8 +15,8 @@
 //        within the EXACT-mode accuracy of the reference's fp32 kernel.
 //
 // Warp roles: 0 producer (one lane issues the TMA / bulk copies), 1 MMA issuer (one lane) and tensor-memory owner,
-// 2..9 decoders (warp d owns n-tiles d, d+8 of the block), 10..13 epilogue (one tensor-memory lane quarter each: raw fp32
-// D rows to global). Every wait is bounded; a timeout sets the workspace error word and all roles leave their loops,
+// 2..9 decoders (warp d owns n-tiles d, d+8 of the block), 10..17 epilogue (two warps per tensor-memory lane quarter,
+// each draining half of the columns: raw fp32 D rows to global). Every wait is bounded; a timeout sets the workspace error word and all roles leave their loops,
 // drain their asynchronous work and free the tensor memory.
 //
 // The numbers are those of the EXACT GEMV path (ft_core.h:313-387 with fp16 weights, fp32 accumulation); the
@@ -33,7 +34,7 @@ namespace {
 
 constexpr int PM = 128;                  // rows per tile (UMMA M)
 constexpr int PK = 64;                   // k per stage (4 UMMA K16 steps, 4 trellis k-rows)
-constexpr int NDEC = 8, NEPI = 4;
+constexpr int NDEC = 8, NEPI = 8;
 constexpr int W_PROD = 0, W_MMA = 1, W_DEC0 = 2, W_EPI0 = W_DEC0 + NDEC;
 constexpr int PTHREADS = (W_EPI0 + NEPI) * 32;
 constexpr int SMEM_MAX = 227 * 1024;
@@ -278,8 +279,6 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         const int d = warp - W_DEC0;
         LaneDecode<K> L;
         L.init(lane);
-        OnesFrag ones;
-        ones.init(lane);
         // stmatrix row address of this lane: matrix j = lane / 8 (0: n 0-7 k 0-7, 1: n 8-15 k 0-7, 2: n 0-7 k 8-15,
         // 3: n 8-15 k 8-15), row = lane % 8; K-major interleaved B: 8-row groups 1024 B apart, 16-byte k-chunks 128 B
         const int j = lane >> 3;
@@ -314,7 +313,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                         lw[i * 4 + kt] = lds32(tile + L.off_lo);
                     }
 #pragma unroll
-                for (int u = 0; u < 4 * NPW; ++u) decode_frag_tc_from<K>(hw[u], lw[u], L, ones, frag[u]);
+                for (int u = 0; u < 4 * NPW; ++u) decode_frag_nat<K>(hw[u], lw[u], L, frag[u]);
 #pragma unroll
                 for (int i = 0; i < NPW; ++i)
 #pragma unroll
@@ -328,6 +327,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     else
     {
         const int q = warp & 3;              // tensor-memory lane quarter this warp may read
+        const int half = (warp - W_EPI0) >> 2;   // two warps per quarter, each drains half of the columns
         const int chains = nks / 2 < C::CH ? nks / 2 : C::CH;
         int lt = 0;
         for (long long t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, ++lt)
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             const bool valid = r < job.z;
             const size_t row = (size_t) job.y + r;
             const uint32_t tq = tmem + ((uint32_t) (32 * q) << 16);
-            for (int c = 0; c < TN / 16; ++c)
+            for (int c = half * (TN / 32); c < (half + 1) * (TN / 32); ++c)
             {
                 // the chains' 16 columns are loaded together and waited for once, then added in chain order
                 uint32_t v[C::CH][16];
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     }
 }
 
-// ---- gate/up epilogue: raw g, u -> out_block, SiLU*up, down input transform (fp16, PERM16 order) ----
+// ---- gate/up epilogue: raw g, u -> out_block, SiLU*up, down input transform (fp16, natural order) ----
 struct EpiPfArgs
 {
     const Plan* plan;
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(256) epi_pf_kernel(EpiPfArgs a)
     for (int q = 0; q < 4; ++q)
     {
         const int c = lane + 32 * q;
-        a.xd[(size_t) row * a.I + nb * 128 + (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(av[q], HAD));
+        a.xd[(size_t) row * a.I + nb * 128 + c] = __float2half_rn(__fmul_rn(av[q], HAD));
     }
 }
 
@@ -533,7 +533,7 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
     cudaError_t e;
     if (rows > 0)
     {
-        if ((e = launch_prep_exact(L, x, x_dtype, ws, lay, st)) != cudaSuccess) return e;
+        if ((e = launch_prep_exact(L, x, x_dtype, ws, lay, st, true)) != cudaSuccess) return e;
         if ((e = mark(2)) != cudaSuccess) return e;
 
         // upper bound of the jobs of <= 128 rows: every expert may end with a partial job
