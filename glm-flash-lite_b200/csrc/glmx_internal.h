@@ -79,8 +79,8 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
                                    const HcOut* hc = nullptr);
 // EXACT input transform of every row (xg, xu: fp16 [R][H]; PERM16 order inside 16-row tiles for the GEMV kernels,
 // natural order for the tensor-core GEMM)
-cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st,
-                              bool natural = false);
+cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, int ntok, int topk, uint8_t* ws, const WsLayout& lay,
+                              cudaStream_t st, bool natural);
 // down out_block of raw fp32 rows [R][H] + weighted sum in pick order (+ shared expert) into out
 cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
                                uint8_t* ws, const WsLayout& lay, cudaStream_t st, const HcOut* hc = nullptr);

@@ -299,14 +299,16 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
 }
 
 // ---- prep: xt = fp16(had128(x * suh) * HAD) per row and projection (gate, up) ----
+// One warp per (token, 128-input block, projection): the token's x block is loaded once and transformed for every row
+// of the token (its routed picks, then the shared expert's row), each with that row's expert's suh.
 struct PrepArgs
 {
     const Plan* plan;
     const void* x; int x_dtype; int H;
-    const int* row_token; const int* row_expert;
+    int ntok, topk, has_shared, E;
+    const int* pick_row; const int* row_expert;
     const __half* suh_g; const __half* suh_u;
     __half* xg; __half* xu;
-    int rows_max;
     int natural;          // 1: natural input order (tensor-core GEMM), 0: PERM16 order inside 16-row tiles (GEMV)
 };
 
@@ -322,25 +324,37 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
     const int nbk = a.H / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const int row = (int) (wid / (2 * nbk));
-    if (row >= a.plan->R) return;
+    const int t = (int) (wid / (2 * nbk));
+    if (t >= a.ntok) return;
     const int rem = (int) (wid % (2 * nbk)), p = rem / nbk, b = rem % nbk;
-    const int t = a.row_token[row], e = a.row_expert[row];
-    const __half* suh = (p ? a.suh_u : a.suh_g) + (size_t) e * a.H + b * 128;
-    float v[4];
+    float xv[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < 4; ++q) xv[q] = load_x(a.x, a.x_dtype, (size_t) t * a.H + b * 128 + lane + 32 * q);
+    const __half* suh_p = p ? a.suh_u : a.suh_g;
+    __half* out_p = p ? a.xu : a.xg;
+    const int nk = a.topk + (a.has_shared ? 1 : 0);
+    for (int k = 0; k < nk; ++k)
     {
-        const int c = lane + 32 * q;
-        v[q] = __fmul_rn(load_x(a.x, a.x_dtype, (size_t) t * a.H + b * 128 + c), __half2float(suh[c]));
-    }
-    had128_warp(v, lane);
-    __half* out = (p ? a.xu : a.xg) + (size_t) row * a.H + b * 128;
+        int r, e;
+        if (k < a.topk)
+        {
+            r = a.pick_row[(size_t) t * a.topk + k];
+            if (r < 0) continue;
+            e = a.row_expert[r];
+        }
+        else { r = a.plan->P + t; e = a.E; }
+        const __half* suh = suh_p + (size_t) e * a.H + b * 128;
+        float v[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-    {
-        const int c = lane + 32 * q;             // GEMV: PERM16 order inside each 16-row tile (decode_frag_tc)
-        out[a.natural ? c : (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
+        for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(xv[q], __half2float(suh[lane + 32 * q]));
+        had128_warp(v, lane);
+        __half* out = out_p + (size_t) r * a.H + b * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+        {
+            const int c = lane + 32 * q;         // GEMV: PERM16 order inside each 16-row tile (decode_frag_tc)
+            out[a.natural ? c : (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
+        }
     }
 }
 
@@ -538,22 +552,21 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     return w;
 }
 
-cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, uint8_t* ws, const WsLayout& lay, cudaStream_t st,
-                              bool natural)
+cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, int ntok, int topk, uint8_t* ws, const WsLayout& lay,
+                              cudaStream_t st, bool natural)
 {
-    const int rows = lay.rows_max;
-    if (rows <= 0) return cudaSuccess;
+    if (ntok <= 0) return cudaSuccess;
     PrepArgs p;
     p.plan = reinterpret_cast<const Plan*>(ws + lay.plan); p.x = x; p.x_dtype = x_dtype; p.H = L.H;
-    p.row_token = reinterpret_cast<const int*>(ws + lay.row_token);
+    p.ntok = ntok; p.topk = topk; p.has_shared = L.has_shared; p.E = L.E;
+    p.pick_row = reinterpret_cast<const int*>(ws + lay.pick_row);
     p.row_expert = reinterpret_cast<const int*>(ws + lay.row_expert);
     p.suh_g = reinterpret_cast<const __half*>(L.suh[0]);
     p.suh_u = reinterpret_cast<const __half*>(L.suh[1]);
     p.xg = reinterpret_cast<__half*>(ws + lay.xg);
     p.xu = reinterpret_cast<__half*>(ws + lay.xu);
-    p.rows_max = rows;
     p.natural = natural ? 1 : 0;
-    const long long warps = (long long) rows * 2 * (L.H / 128);
+    const long long warps = (long long) ntok * 2 * (L.H / 128);
     prep_kernel<<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(p);
     return cudaGetLastError();
 }
@@ -572,18 +585,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
     cudaError_t e;
     if (rows > 0)
     {
-        PrepArgs p;
-        p.plan = plan; p.x = x; p.x_dtype = x_dtype; p.H = L.H;
-        p.row_token = reinterpret_cast<const int*>(ws + lay.row_token);
-        p.row_expert = reinterpret_cast<const int*>(ws + lay.row_expert);
-        p.suh_g = reinterpret_cast<const __half*>(L.suh[0]);
-        p.suh_u = reinterpret_cast<const __half*>(L.suh[1]);
-        p.xg = reinterpret_cast<__half*>(ws + lay.xg);
-        p.xu = reinterpret_cast<__half*>(ws + lay.xu);
-        p.rows_max = rows;
-        const long long warps = (long long) rows * 2 * (L.H / 128);
-        prep_kernel<<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_prep_exact(L, x, x_dtype, ntok, topk, ws, lay, st, false)) != cudaSuccess) return e;
         if ((e = mark(2)) != cudaSuccess) return e;
 
         GemvArgs g;
@@ -595,7 +597,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
         g.act_limit = L.act_limit;
         // gate + up
         g.proj0 = 0; g.kt = L.H / 16; g.ntn = L.I / 16; g.kdim = L.H; g.ndim = L.I;
-        g.xin0 = p.xg; g.xin1 = p.xu;
+        g.xin0 = reinterpret_cast<const __half*>(ws + lay.xg); g.xin1 = reinterpret_cast<const __half*>(ws + lay.xu);
         g.svh0 = reinterpret_cast<const __half*>(L.svh[0]);
         g.svh1 = reinterpret_cast<const __half*>(L.svh[1]);
         g.suh_next = reinterpret_cast<const __half*>(L.suh[2]);

@@ -533,7 +533,7 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
     cudaError_t e;
     if (rows > 0)
     {
-        if ((e = launch_prep_exact(L, x, x_dtype, ws, lay, st, true)) != cudaSuccess) return e;
+        if ((e = launch_prep_exact(L, x, x_dtype, ntok, topk, ws, lay, st, true)) != cudaSuccess) return e;
         if ((e = mark(2)) != cudaSuccess) return e;
 
         // upper bound of the jobs of <= 128 rows: every expert may end with a partial job
