@@ -404,17 +404,25 @@ __global__ void __launch_bounds__(256) epi_pf_kernel(EpiPfArgs a)
     const int nb = (int) (wid % nbk);
     const int e = a.row_expert[row];
     const size_t cb = (size_t) e * a.I + nb * 128;
+    // every partial is read once: issue all the loads (streaming), then add the splits in order
+    float gp[PF_KSPLIT][4], up[PF_KSPLIT][4];
+#pragma unroll
+    for (int s = 0; s < PF_KSPLIT; ++s)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+        {
+            const size_t o = s * a.split_stride + (size_t) row * 2 * a.I + nb * 128 + lane + 32 * q;
+            gp[s][q] = s < a.ksplit ? __ldcs(a.yraw + o) : 0.0f;
+            up[s][q] = s < a.ksplit ? __ldcs(a.yraw + o + a.I) : 0.0f;
+        }
     float gv[4], uv[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q)
     {
-        const size_t o = (size_t) row * 2 * a.I + nb * 128 + lane + 32 * q;
-        float g = a.yraw[o], u = a.yraw[o + a.I];
-        for (int s = 1; s < a.ksplit; ++s)
-        {
-            g = __fadd_rn(g, a.yraw[s * a.split_stride + o]);
-            u = __fadd_rn(u, a.yraw[s * a.split_stride + o + a.I]);
-        }
+        float g = gp[0][q], u = up[0][q];
+#pragma unroll
+        for (int s = 1; s < PF_KSPLIT; ++s)
+            if (s < a.ksplit) { g = __fadd_rn(g, gp[s][q]); u = __fadd_rn(u, up[s][q]); }
         gv[q] = r16(g);
         uv[q] = r16(u);
     }
