@@ -15,8 +15,9 @@
 //        within the EXACT-mode accuracy of the reference's fp32 kernel.
 //
 // Warp roles: 0 producer (one lane issues the TMA / bulk copies), 1 MMA issuer (one lane) and tensor-memory owner,
-// 2..9 decoders (warp d owns n-tiles d, d+8 of the block), 10..17 epilogue (two warps per tensor-memory lane quarter,
-// each draining half of the columns: raw fp32 D rows to global). Every wait is bounded; a timeout sets the workspace error word and all roles leave their loops,
+// 2.. decoders (16 with TN = 256, 8 with TN = 128; warp d decodes tiles d, d + NDEC, ... of the stage's 4 x TN/16),
+// then 8 epilogue warps (two per tensor-memory lane quarter, each draining half of the columns: raw fp32 D rows to
+// global). Every wait is bounded; a timeout sets the workspace error word and all roles leave their loops,
 // drain their asynchronous work and free the tensor memory.
 //
 // The numbers are those of the EXACT GEMV path (ft_core.h:313-387 with fp16 weights, fp32 accumulation); the
@@ -34,9 +35,8 @@ namespace {
 
 constexpr int PM = 128;                  // rows per tile (UMMA M)
 constexpr int PK = 64;                   // k per stage (4 UMMA K16 steps, 4 trellis k-rows)
-constexpr int NDEC = 8, NEPI = 8;
-constexpr int W_PROD = 0, W_MMA = 1, W_DEC0 = 2, W_EPI0 = W_DEC0 + NDEC;
-constexpr int PTHREADS = (W_EPI0 + NEPI) * 32;
+constexpr int NEPI = 8;
+constexpr int W_PROD = 0, W_MMA = 1, W_DEC0 = 2;
 constexpr int SMEM_MAX = 227 * 1024;
 // kind::f16 instruction descriptor: D f32 (bit 4), A = B = f16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24
 __host__ __device__ constexpr uint32_t idesc_f16(int n) { return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (PM >> 4) << 24); }
@@ -57,6 +57,10 @@ struct CfgP
     static constexpr int SMEM = 1024 + NST * STAGE + BAR_BYTES;   // 1024: alignment slack of the swizzled A tiles
     static constexpr int TMEM_COLS = 512;
     static constexpr int CH = TMEM_COLS / TN;                      // accumulator chains
+    // decoder warps: 16 with TN = 256 (4 tiles each per stage); 8 with TN = 128, whose epilogue needs the registers
+    static constexpr int NDEC = TN == 256 ? 16 : 8;
+    static constexpr int W_EPI0 = W_DEC0 + NDEC;
+    static constexpr int THREADS = (W_EPI0 + NEPI) * 32;
     static_assert(STAGE % 1024 == 0, "A tiles must stay 1024-byte aligned");
     static_assert(NST >= 2, "at least two stages");
     static_assert(SMEM <= SMEM_MAX, "shared memory");
@@ -155,7 +159,7 @@ __device__ __forceinline__ PfTile pf_tile(long long t, int NB, int NP, int KS)
 }
 
 template <int K, int TN>
-__global__ void __launch_bounds__(PTHREADS, 1)
+__global__ void __launch_bounds__(CfgP<K, TN>::THREADS, 1)
     gemm_pf_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1, PfArgs a)
 {
     using C = CfgP<K, TN>;
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0)
     {
-        for (int s = 0; s < C::NST; ++s) { mbar_init(&full[s], 1); mbar_init(&dec[s], NDEC); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < C::NST; ++s) { mbar_init(&full[s], 1); mbar_init(&dec[s], C::NDEC); mbar_init(&empty[s], 1); }
         mbar_init(tfull, 1);
         mbar_init(tempty, NEPI);
         mbar_init(fin, 1);
@@ -272,22 +276,26 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             if (!mbar_wait_bounded(fin, 0)) atomicOr(a.err, ERR_TIMEOUT_FULL);
         }
     }
-    else if (warp < W_EPI0)
+    else if (warp < C::W_EPI0)
     {
         // decoders: warp d owns n-tiles d, d + 8, ... of the column block; per stage it decodes their 4 k-tiles
-        constexpr int NPW = C::NT / NDEC;              // n-tiles per decoder warp
+        constexpr int TPW = 4 * C::NT / C::NDEC;       // tiles per decoder warp and stage: tile u = d + NDEC i
+        static_assert(TPW >= 1 && (4 * C::NT) % C::NDEC == 0, "decoder split");
         const int d = warp - W_DEC0;
         LaneDecode<K> L;
         L.init(lane);
         // stmatrix row address of this lane: matrix j = lane / 8 (0: n 0-7 k 0-7, 1: n 8-15 k 0-7, 2: n 0-7 k 8-15,
-        // 3: n 8-15 k 8-15), row = lane % 8; K-major interleaved B: 8-row groups 1024 B apart, 16-byte k-chunks 128 B
+        // 3: n 8-15 k 8-15), row = lane % 8; K-major interleaved B: 8-row groups 1024 B apart, 16-byte k-chunks 128 B,
+        // the stage's k-tile kt 256 B further
         const int j = lane >> 3;
-        uint32_t boff[NPW];
+        uint32_t boff[TPW], toff[TPW];
 #pragma unroll
-        for (int i = 0; i < NPW; ++i)
+        for (int i = 0; i < TPW; ++i)
         {
-            const int n = 16 * (d + NDEC * i) + (lane & 7) + 8 * (j & 1);
-            boff[i] = (uint32_t) ((n >> 3) * 1024 + (j >> 1) * 128 + (n & 7) * 16);
+            const int u = d + C::NDEC * i, nt = u % C::NT, kt = u / C::NT;
+            const int n = 16 * nt + (lane & 7) + 8 * (j & 1);
+            boff[i] = (uint32_t) ((n >> 3) * 1024 + (j >> 1) * 128 + (n & 7) * 16 + kt * 256);
+            toff[i] = (uint32_t) ((kt * C::NT + nt) * (32 * K));
         }
         long long it = 0;
         for (long long t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x)
@@ -302,22 +310,17 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                 const uint8_t* tr = st + C::TA + C::TB;
                 const uint32_t sb = smem_u32(st + C::TA);
                 // all loads first, then independent decode chains, then the stores
-                uint32_t hw[4 * NPW], lw[4 * NPW], frag[4 * NPW][4];
+                uint32_t hw[TPW], lw[TPW], frag[TPW][4];
 #pragma unroll
-                for (int i = 0; i < NPW; ++i)
+                for (int i = 0; i < TPW; ++i)
+                {
+                    hw[i] = lds32(tr + toff[i] + L.off_hi);
+                    lw[i] = lds32(tr + toff[i] + L.off_lo);
+                }
 #pragma unroll
-                    for (int kt = 0; kt < 4; ++kt)
-                    {
-                        const uint8_t* tile = tr + (kt * C::NT + d + NDEC * i) * (32 * K);
-                        hw[i * 4 + kt] = lds32(tile + L.off_hi);
-                        lw[i * 4 + kt] = lds32(tile + L.off_lo);
-                    }
+                for (int i = 0; i < TPW; ++i) decode_frag_nat<K>(hw[i], lw[i], L, frag[i]);
 #pragma unroll
-                for (int u = 0; u < 4 * NPW; ++u) decode_frag_nat<K>(hw[u], lw[u], L, frag[u]);
-#pragma unroll
-                for (int i = 0; i < NPW; ++i)
-#pragma unroll
-                    for (int kt = 0; kt < 4; ++kt) stmatrix_x4(sb + boff[i] + kt * 256, frag[i * 4 + kt]);
+                for (int i = 0; i < TPW; ++i) stmatrix_x4(sb + boff[i], frag[i]);
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&dec[s]);
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     else
     {
         const int q = warp & 3;              // tensor-memory lane quarter this warp may read
-        const int half = (warp - W_EPI0) >> 2;   // two warps per quarter, each drains half of the columns
+        const int half = (warp - C::W_EPI0) >> 2;   // two warps per quarter, each drains half of the columns
         const int chains = nks / 2 < C::CH ? nks / 2 : C::CH;
         int lt = 0;
         for (long long t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, ++lt)
@@ -498,7 +501,7 @@ cudaError_t launch_gemm_pf(const Layer& L, const CUtensorMap& m0, const CUtensor
     }
     const long long grid = max_tiles < sms[L.device] ? max_tiles : sms[L.device];
     if (grid <= 0) return cudaSuccess;
-    gemm_pf_kernel<K, TN><<<(unsigned) grid, PTHREADS, C::SMEM, st>>>(m0, m1, a);
+    gemm_pf_kernel<K, TN><<<(unsigned) grid, C::THREADS, C::SMEM, st>>>(m0, m1, a);
     return cudaGetLastError();
 }
 
