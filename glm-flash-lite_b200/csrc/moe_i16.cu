@@ -363,6 +363,37 @@ struct CombineI16Args
     HcOut hc;                           // hc.x != nullptr: hyper-connection epilogue instead of writing out
 };
 
+// the combined value of token t, columns hb*128 + lane + 32q: hyper-connection update or (accumulating) store
+__device__ __forceinline__ void combine_store(const CombineI16Args& a, int t, int hb, int lane, const float acc[4])
+{
+    if (a.hc.x)
+    {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+        {
+            const float y = a.hc.y_half ? __half2float(__float2half_rn(acc[q])) : acc[q];
+            hc_apply_col(a.hc.x + (size_t) t * 4 * a.H, a.H, hb * 128 + lane + 32 * q, y, a.hc.post + (size_t) t * 4,
+                         a.hc.comb + (size_t) t * 16);
+        }
+        return;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+    {
+        const size_t o = (size_t) t * a.H + hb * 128 + lane + 32 * q;
+        if (a.out_dtype == GLMX_F32)
+        {
+            float* p = reinterpret_cast<float*>(a.out) + o;
+            *p = a.accumulate ? __fadd_rn(*p, acc[q]) : acc[q];
+        }
+        else
+        {
+            __half* p = reinterpret_cast<__half*>(a.out) + o;
+            *p = __float2half_rn(a.accumulate ? __fadd_rn(__half2float(*p), acc[q]) : acc[q]);
+        }
+    }
+}
+
 // one warp per (token, 128-output block): down out_block per pick, weighted sum in pick order (+ shared)
 __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
 {
@@ -398,32 +429,74 @@ __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
             acc[q] = k < a.topk ? __fadd_rn(acc[q], __fmul_rn(w, yq)) : __fadd_rn(acc[q], yq);
         }
     }
-    if (a.hc.x)
+    combine_store(a, t, hb, lane, acc);
+}
+
+// Small batches: one CTA per (token, 128-output block), one warp per pick computing its weighted down out_block into
+// shared memory; warp 0 then adds the picks in pick order (the same fp32 operations as combine_i16_kernel, in the
+// same order), so the picks' transforms run side by side instead of one after another.
+constexpr int COMBINE_MAXK = 65;           // topk <= 64, plus the shared expert
+constexpr int COMBINE_WIDE_MAX_TOKENS = 32;
+__global__ void __launch_bounds__(256) combine_wide_kernel(CombineI16Args a)
+{
+    __shared__ float ys[COMBINE_MAXK][128];
+    __shared__ int valid[COMBINE_MAXK];
+    const int nbk = a.H / 128;
+    const int t = blockIdx.x / nbk, hb = blockIdx.x % nbk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = a.topk + (a.has_shared ? 1 : 0);
+    for (int k = warp; k < nk; k += 8)
     {
+        int r;
+        float w = 1.0f;
+        if (k < a.topk)
+        {
+            r = a.pick_row[t * a.topk + k];
+            if (r < 0)
+            {
+                if (lane == 0) valid[k] = 0;
+                continue;
+            }
+            w = a.row_weight[r];
+        }
+        else r = a.plan->P + t;
+        const int e = k < a.topk ? a.row_expert[r] : a.E;
+        float y[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) y[q] = r16(a.yraw[(size_t) r * a.H + hb * 128 + lane + 32 * q]);
+        had128_warp(y, lane);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
         {
-            const float y = a.hc.y_half ? __half2float(__float2half_rn(acc[q])) : acc[q];
-            hc_apply_col(a.hc.x + (size_t) t * 4 * a.H, a.H, hb * 128 + lane + 32 * q, y, a.hc.post + (size_t) t * 4,
-                         a.hc.comb + (size_t) t * 16);
+            const int c = hb * 128 + lane + 32 * q;
+            const float yq = r16(__fmul_rn(__fmul_rn(y[q], HAD), __half2float(a.svh_d[(size_t) e * a.H + c])));
+            ys[k][lane + 32 * q] = k < a.topk ? __fmul_rn(w, yq) : yq;
         }
-        return;
+        if (lane == 0) valid[k] = 1;
     }
+    __syncthreads();
+    if (warp != 0) return;
+    float acc[4] = { 0.f, 0.f, 0.f, 0.f };
+    for (int k = 0; k < nk; ++k)
+        if (valid[k])
+        {
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < 4; ++q) acc[q] = __fadd_rn(acc[q], ys[k][lane + 32 * q]);
+        }
+    combine_store(a, t, hb, lane, acc);
+}
+
+// the combine for ntok tokens: the wide form at decode sizes, one warp per (token, block) above
+cudaError_t launch_combine(const CombineI16Args& c, int ntok, int H, cudaStream_t st)
+{
+    if (ntok <= COMBINE_WIDE_MAX_TOKENS)
+        combine_wide_kernel<<<(unsigned) (ntok * (H / 128)), 256, 0, st>>>(c);
+    else
     {
-        const size_t o = (size_t) t * a.H + hb * 128 + lane + 32 * q;
-        if (a.out_dtype == GLMX_F32)
-        {
-            float* p = reinterpret_cast<float*>(a.out) + o;
-            *p = a.accumulate ? __fadd_rn(*p, acc[q]) : acc[q];
-        }
-        else
-        {
-            __half* p = reinterpret_cast<__half*>(a.out) + o;
-            *p = __float2half_rn(a.accumulate ? __fadd_rn(__half2float(*p), acc[q]) : acc[q]);
-        }
+        const long long w3 = (long long) ntok * (H / 128);
+        combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
     }
+    return cudaGetLastError();
 }
 
 template <int K0, int K1, int NMAT>
@@ -471,9 +544,7 @@ cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int 
     c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared; c.E = L.E;
     c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
     c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
-    const long long w3 = (long long) ntok * (L.H / 128);
-    combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
-    return cudaGetLastError();
+    return launch_combine(c, ntok, L.H, st);
 }
 
 cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, void* out, int out_dtype,
@@ -568,9 +639,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         c.H = L.H; c.ntok = ntok; c.topk = topk; c.has_shared = L.has_shared; c.E = L.E;
         c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
         c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
-        const long long w3 = (long long) ntok * (L.H / 128);
-        combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_combine(c, ntok, L.H, st)) != cudaSuccess) return e;
     }
     return mark(5);
 }
