@@ -548,6 +548,8 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.actb_d = take((size_t) ji * BI * I16_ACT_BYTES);
     w.sc_d = take(sizeof(float) * 4 * (size_t) ji * BI);
     w.psum_d = take(sizeof(float) * (size_t) (ji ? rows : 0) * BI);
+    // K-split class sums of the I16 gate/up GEMV for calls of at most I16_SPLIT_MAX_ROWS rows
+    w.isum_gu = take(ji && rows <= I16_SPLIT_MAX_ROWS ? sizeof(int) * 4 * (size_t) rows * 2 * BH * L.I : 0);
     w.total = o;
     return w;
 }

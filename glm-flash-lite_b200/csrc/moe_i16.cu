@@ -62,9 +62,68 @@ struct GemvI16Args
     const float* psum;              // [R][nmat][kt/8]
     float* yraw;                    // [R][nmat][ndim]
     int* err;
+    // K split of small calls (gate+up, at most I16_SPLIT_MAX_ROWS rows): each split stores its exact int32 class sums
+    // per 128-input block, isum [R][nmat][kt/8][ndim][4 classes]; the last split of a (job, column block) to arrive
+    // (counters [J][ndim/128], cleared by the route kernel) runs the per-class fp32 chains in block order
+    int* isum;
+    int* counters;
 };
 
-template <int K0, int K1, int NMAT>
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory"); }
+
+// y of one (row, projection, column) from its exact block sums: the four class chains a_c = fma(float(I_b,c), sc_b,
+// a_c) in block order, then KINV * ((a0 + a1) + (a2 + a3)) + CAFF * sumx, as the unsplit kernel does
+__device__ __forceinline__ float i16_finish(float a0, float a1, float a2, float a3, const float* ps, int nkb)
+{
+    const float kinv = __half2float(__ushort_as_half(KINV_BITS));
+    const float caff = 1024.0f * kinv + __half2float(__ushort_as_half(KBIAS_BITS));
+    float sumx = 0.0f;
+    for (int kb0 = 0; kb0 < nkb; kb0 += 8)
+    {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = kb0 + u < nkb ? __ldg(ps + kb0 + u) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (kb0 + u < nkb) sumx = __fadd_rn(sumx, v[u]);
+    }
+    const float lo = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+    return __fadd_rn(__fmul_rn(kinv, lo), __fmul_rn(caff, sumx));
+}
+
+// The last split of a (job, column block): every (row slot, projection, column) of the block from the stored block
+// sums. Kept out of line so its registers do not weigh on the main loop's allocation.
+__device__ __noinline__ void i16_chain_item(const GemvI16Args& a, int4 job, int j, int nbi, int nmat, int nkb, int tid)
+{
+    for (int idx = tid; idx < job.z * nmat * 128; idx += NW * 32)
+    {
+        const int slot = idx / (nmat * 128), m = (idx / 128) % nmat, col = nbi * 128 + idx % 128;
+        const int row = job.y + slot;
+        const int4* src = reinterpret_cast<const int4*>(a.isum) + (((size_t) row * nmat + m) * nkb) * a.ndim + col;
+        const float* scl = a.scales + ((size_t) j * nmat + m) * nkb * 4 + slot;
+        float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+        for (int kb0 = 0; kb0 < nkb; kb0 += 4)
+        {
+            int4 v[4];
+            float sc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (kb0 + u < nkb) { v[u] = __ldcg(src + (size_t) (kb0 + u) * a.ndim); sc[u] = __ldg(scl + (kb0 + u) * 4); }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (kb0 + u < nkb)
+                {
+                    c0 = __fmaf_rn(__int2float_rn(v[u].x), sc[u], c0);
+                    c1 = __fmaf_rn(__int2float_rn(v[u].y), sc[u], c1);
+                    c2 = __fmaf_rn(__int2float_rn(v[u].z), sc[u], c2);
+                    c3 = __fmaf_rn(__int2float_rn(v[u].w), sc[u], c3);
+                }
+        }
+        a.yraw[((size_t) row * nmat + m) * a.ndim + col] = i16_finish(c0, c1, c2, c3, a.psum + ((size_t) row * nmat + m) * nkb, nkb);
+    }
+}
+
+template <int K0, int K1, int NMAT, bool SPLIT>
 __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
 {
     using C = CfgI<K0, K1, NMAT>;
@@ -84,7 +143,10 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
     const Plan pl = *a.plan;
     const int nb = a.ntn / NW;
     const int nkb = a.kt / RB;
-    const long long items = (long long) pl.J * nb;
+    const int S = SPLIT ? pl.S_gu : 1;                                       // K splits (item = (job, block, split))
+    const int kbs = nkb / S;                                                 // blocks per split
+    const long long items = (long long) pl.J * nb * S;
+    __shared__ int s_last;
 
     if (warp == NW)
     {
@@ -92,11 +154,13 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
         long long it = 0;
         for (long long item = blockIdx.x; item < items && !s_abort; item += gridDim.x)
         {
-            const int nbi = (int) (item % nb), j = (int) (item / nb);
+            const int ks = (int) (item % S);
+            const long long jn = item / S;
+            const int nbi = (int) (jn % nb), j = (int) (jn / nb);
             const int4 job = a.jobs[j];
             const uint8_t* b0 = reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0]);
             const uint8_t* b1 = NMAT > 1 ? reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0 + 1]) : nullptr;
-            for (int kb = 0; kb < nkb; ++kb, ++it)
+            for (int kb = ks * kbs; kb < (ks + 1) * kbs; ++kb, ++it)
             {
                 const int s = (int) (it % C::NST);
                 const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
@@ -136,7 +200,9 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
     long long it = 0;
     for (long long item = blockIdx.x; item < items; item += gridDim.x)
     {
-        const int nbi = (int) (item % nb), j = (int) (item / nb);
+        const int ks = (int) (item % S);
+        const long long jn = item / S;
+        const int nbi = (int) (jn % nb), j = (int) (jn / nb);
         const int4 job = a.jobs[j];
         float accf[NMAT][4][2];
 #pragma unroll
@@ -144,7 +210,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
 #pragma unroll
             for (int c = 0; c < 4; ++c) accf[m][c][0] = accf[m][c][1] = 0.0f;
 
-        for (int kb = 0; kb < nkb; ++kb, ++it)
+        for (int kb = ks * kbs; kb < (ks + 1) * kbs; ++kb, ++it)
         {
             const int s = (int) (it % C::NST);
             const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
@@ -181,18 +247,46 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                         imma_u8s8(acc[c], xa[c], xa[c + 4], xb[c], xb[c + 4], bb.x, bb.y);
                     }
                 }
-                const float sc = *reinterpret_cast<const float*>(st + C::MAT0 + C::MAT1 + C::ACT + m * 16 + tq * 4);
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
+                if (SPLIT && S > 1)
+                {
+                    // exact class sums of this block for row slot tq, columns g and g + 8 of the warp's n-tile
+                    if (tq < job.z)
                     {
-                        const int v = acc[c][2 * h] * 256 + acc[c][2 * h + 1];     // exact: |v| < 2^30
-                        accf[m][c][h] = __fmaf_rn(__int2float_rn(v), sc, accf[m][c][h]);
+                        int* dst = a.isum + ((((size_t) (job.y + tq) * NMAT + m) * nkb + kb) * a.ndim + nbi * 128 + warp * 16 + g) * 4;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            __stcg(reinterpret_cast<int4*>(dst + 32 * h),
+                                   make_int4(acc[0][2 * h] * 256 + acc[0][2 * h + 1], acc[1][2 * h] * 256 + acc[1][2 * h + 1],
+                                             acc[2][2 * h] * 256 + acc[2][2 * h + 1], acc[3][2 * h] * 256 + acc[3][2 * h + 1]));
                     }
+                }
+                else
+                {
+                    const float sc = *reinterpret_cast<const float*>(st + C::MAT0 + C::MAT1 + C::ACT + m * 16 + tq * 4);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                        {
+                            const int v = acc[c][2 * h] * 256 + acc[c][2 * h + 1];     // exact: |v| < 2^30
+                            accf[m][c][h] = __fmaf_rn(__int2float_rn(v), sc, accf[m][c][h]);
+                        }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (SPLIT && S > 1)
+        {
+            // the last split of this (job, column block) to arrive chains every block's sums, in block order
+            __threadfence();
+            consumers_sync();
+            if (tid == 0) s_last = atomicAdd(a.counters + jn, 1) == S - 1;
+            consumers_sync();
+            if (!s_last) continue;
+            __threadfence();
+            i16_chain_item(a, job, j, nbi, NMAT, nkb, tid);
+            continue;
         }
         if (tq < job.z)
         {
@@ -499,22 +593,30 @@ cudaError_t launch_combine(const CombineI16Args& c, int ntok, int H, cudaStream_
     return cudaGetLastError();
 }
 
-template <int K0, int K1, int NMAT>
-cudaError_t launch_gemv_i16(const Layer& L, const GemvI16Args& a, cudaStream_t st)
+template <int K0, int K1, int NMAT, bool SPLIT>
+cudaError_t launch_gemv_i16_v(const Layer& L, const GemvI16Args& a, cudaStream_t st)
 {
     using C = CfgI<K0, K1, NMAT>;
     static bool attr_set[64] = {};
     static int sms[64] = {};
     if (!attr_set[L.device])
     {
-        cudaError_t e = cudaFuncSetAttribute(gemv_i16_kernel<K0, K1, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemv_i16_kernel<K0, K1, NMAT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         if (cudaDeviceGetAttribute(&sms[L.device], cudaDevAttrMultiProcessorCount, L.device) != cudaSuccess || sms[L.device] <= 0)
             sms[L.device] = 148;
         attr_set[L.device] = true;
     }
-    gemv_i16_kernel<K0, K1, NMAT><<<sms[L.device] * CTAS, NTHR, C::SMEM, st>>>(a);
+    gemv_i16_kernel<K0, K1, NMAT, SPLIT><<<sms[L.device] * CTAS, NTHR, C::SMEM, st>>>(a);
     return cudaGetLastError();
+}
+
+// the K-split form only where its sums buffer exists (gate/up of calls with at most I16_SPLIT_MAX_ROWS rows)
+template <int K0, int K1, int NMAT>
+cudaError_t launch_gemv_i16(const Layer& L, const GemvI16Args& a, cudaStream_t st)
+{
+    if (NMAT == 2 && a.isum) return launch_gemv_i16_v<K0, K1, NMAT, NMAT == 2>(L, a, st);
+    return launch_gemv_i16_v<K0, K1, NMAT, false>(L, a, st);
 }
 
 template <int K0>
@@ -584,6 +686,8 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         g.scales = reinterpret_cast<const float*>(ws + lay.sc_gu);
         g.psum = reinterpret_cast<const float*>(ws + lay.psum_gu);
         g.yraw = reinterpret_cast<float*>(ws + lay.yraw_gu);
+        g.isum = rows <= I16_SPLIT_MAX_ROWS ? reinterpret_cast<int*>(ws + lay.isum_gu) : nullptr;
+        g.counters = reinterpret_cast<int*>(ws + lay.cnt_gu);
         switch (L.bits[0])
         {
             case 2: e = launch_gu_i16_k0<2>(L, g, st); break;
@@ -613,6 +717,8 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         d.scales = reinterpret_cast<const float*>(ws + lay.sc_d);
         d.psum = reinterpret_cast<const float*>(ws + lay.psum_d);
         d.yraw = reinterpret_cast<float*>(ws + lay.yrow);
+        d.isum = nullptr;                       // the down GEMV has J x H/128 column blocks: enough items unsplit
+        d.counters = nullptr;
         switch (L.bits[2])
         {
             case 2: e = launch_gemv_i16<2, 2, 1>(L, d, st); break;

@@ -87,18 +87,22 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total)
 
 // Split-K factor: the smallest divisor d of `stages` (each part >= 2 stages) with units * d >= target, never more
 // items than `slots` partial-sum slots.
+// K splits of a GEMV with `units` (job, column block) items of `stages` 128-input steps on `target` resident CTAs:
+// the divisor d of stages with the shortest critical path, ceil(units * d / target) waves of stages / d steps each
+// (the smaller d on ties, and units * d within the partial-sum slots)
 __device__ int pick_split(long long units, int stages, int target, int slots)
 {
-    int s = 1;
-    if (units >= target) return 1;
-    for (int d = 2; d <= stages / 2; ++d)
+    if (units <= 0 || units >= target) return 1;
+    int best = 1;
+    long long best_cost = stages;
+    for (int d = 2; d <= stages; ++d)
     {
         if (stages % d) continue;
         if (units * d > slots) break;
-        s = d;
-        if (units * d >= target) break;
+        const long long cost = ((units * d + target - 1) / target) * (stages / d);
+        if (cost < best_cost) { best_cost = cost; best = d; }
     }
-    return s;
+    return best;
 }
 
 __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
