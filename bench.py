@@ -524,7 +524,7 @@ def run_expert_parallel(args, rank, world, dev, dist):
 
     tr, ptrs, suh, svh = bank_of(n + 1)          # the shard's n experts + the shared expert (local id n)
     local = MoELayer(H, I, n + 1, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev)
-    layer = ep.ExpertParallelLayer(local, first, n, has_shared=True, E=E)
+    layer = ep.ExpertParallelLayer(local, first, n, has_shared=True, E=E, peer=args.peer)
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
 
@@ -582,8 +582,13 @@ def run_expert_parallel(args, rank, world, dev, dist):
 
     E_ms = timed(e2e_step, args.steps, args.warmup)
     dist.barrier()
+    peer = layer.peer
+    peer_err = layer._ret.error_flags() if peer and layer._ret is not None else 0
+    layer.close()
     del layer
     dist.destroy_process_group()
+    if peer_err:
+        raise RuntimeError(f"peer return error flags {peer_err}")
     if rank != 0:
         return
     peak = pk["hbm_gbs"] * world
@@ -596,6 +601,7 @@ def run_expert_parallel(args, rank, world, dev, dist):
                                f"experts split {n}/GPU + replicated shared expert, H=6144, I=1536, K=3, top-8",
                    "batch": Bg, "tokens_per_gpu": b, "experts_per_gpu": n, "H": H, "I": I, "bits": 3, "topk": TOPK,
                    "mode": {1: "EXACT", 2: "I16"}[args.mode], "parallelism": f"ep{world}",
+                   "return": "peer memory, fused into the combine" if peer else "NCCL reduce-scatter",
                    "l2": "inputs larger than L2 (touched trellis per step > 126 MB)"},
         "hbm_gbs_layer": layer_gbs,
         "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer step (all ranks)", "achieved": layer_gbs,
@@ -605,7 +611,8 @@ def run_expert_parallel(args, rank, world, dev, dist):
         "e2e": {"value": Bg * args.steps / (E_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": world * (b * H * 2 + b * TOPK * 8),
                 "d2h_bytes_per_step": world * b * H * 4},
         # per step and rank: split + transform + gate/up + epilogue + down + combine (the shared expert rides along)
-        "gpu_launches": (6 if args.mode == 2 else 5) * args.steps * world,
+        # (+ the owner's sum of the peer partials)
+        "gpu_launches": ((6 if args.mode == 2 else 5) + (1 if peer else 0)) * args.steps * world,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -620,6 +627,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--peer", action="store_true", help="expert parallelism: return the partials with the combine's "
+                    "peer-memory stores instead of NCCL's reduce-scatter")
     ap.add_argument("--sweep", default="1,8,32", help="extra decode batches measured (device time only)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--experts", type=int, default=E, help="routed experts of the layer (288 = BASELINE)")

@@ -8,7 +8,7 @@ OBJ="$HERE/_build"
 mkdir -p "$OUT" "$OBJ"
 FLAGS=(-std=c++17 -O3 -lineinfo -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC -Xcompiler -fvisibility=hidden
        --expt-relaxed-constexpr -I"$HERE/../include" ${GLMX_NVCC_EXTRA:-})
-SRCS=(route.cu moe_decode.cu moe_i16.cu moe_prefill.cu capi.cu noalloc.cu selftest.cu router.cu)
+SRCS=(route.cu moe_decode.cu moe_i16.cu moe_prefill.cu capi.cu noalloc.cu selftest.cu router.cu peer.cu)
 objs=()
 for s in "${SRCS[@]}"; do
   o="$OBJ/${s%.cu}.o"

@@ -233,6 +233,21 @@ int glmx_moe_forward_hc(const glmx_layer* l, const void* x, int x_dtype, int nto
                         nullptr, &hc);
 }
 
+int glmx_moe_forward_peer(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                          const void* w, int w_dtype, int topk, int mode, const glmx_peer_out* peer, void* ws, size_t ws_bytes,
+                          void* stream)
+{
+    if (!peer || !peer->recv || !peer->flags || !peer->counter) return fail(GLMX_E_ARG, "glmx_moe_forward_peer: null peer table");
+    if (peer->world < 1 || peer->world > 64 || peer->rank < 0 || peer->rank >= peer->world || peer->rows_per_rank <= 0 ||
+        peer->seq <= 0 || (long long) peer->world * peer->rows_per_rank != ntok)
+        return fail(GLMX_E_ARG, "glmx_moe_forward_peer: need 0 <= rank < world <= 64, seq > 0 and ntok = world * rows_per_rank > 0");
+    HcOut hc{};
+    hc.peer = PeerOut{ reinterpret_cast<float* const*>(peer->recv), peer->flags, peer->counter, peer->rank, peer->world,
+                       peer->rows_per_rank, peer->seq };
+    return forward_impl(l, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, nullptr, GLMX_F32, 0, ws, ws_bytes, stream,
+                        nullptr, &hc);
+}
+
 int glmx_decode_tiles(const uint8_t* tiles, int bits, int ntiles, uint16_t* out, void* stream)
 {
     if (bits < 2 || bits > 4) return fail(GLMX_E_ARG, "glmx_decode_tiles: bits must be 2, 3 or 4");

@@ -20,7 +20,7 @@ constexpr int MAXM = 8;                         // tokens per job (ft_core.h:32)
 constexpr int WAIT_TIMEOUT_NS = 2000000000;     // bounded device waits: 2 s
 
 // error bits written to the workspace error word
-enum : int { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_BAD_EXPERT = 4, ERR_BAD_SHAPE = 8 };
+enum : int { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_BAD_EXPERT = 4, ERR_BAD_SHAPE = 8, ERR_TIMEOUT_PEER = 16 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -87,6 +87,46 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
+}
+
+// ---- expert-parallel return over peer memory ------------------------------------------------------------------------
+
+__device__ __forceinline__ void st_release_sys(int* p, int v)
+{
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p)
+{
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Destination of token t's combined row in the peer return (see PeerOut).
+__device__ __forceinline__ float* peer_row(float* const* recv, int rank, int world, int rpr, int seq, int t, int H)
+{
+    const int owner = t / rpr, tl = t % rpr;
+    return recv[owner] + ((size_t) ((seq & 1) * world + rank) * rpr + tl) * H;
+}
+
+// Called by every thread of every CTA of a combine launch after its peer stores: the last CTA to arrive (arrival
+// counter, no waiting) publishes flag [seq & 1][rank] = seq on every rank and clears the counter.
+__device__ __forceinline__ void peer_done(float* const* recv, int* const* flags, int* counter, int rank, int world, int seq)
+{
+    (void) recv;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && threadIdx.y == 0)
+    {
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        if ((unsigned) atomicAdd(counter, 1) == total - 1)
+        {
+            __threadfence_system();
+            for (int d = 0; d < world; ++d) st_release_sys(flags[d] + (seq & 1) * world + rank, seq);
+            atomicExch(counter, 0);
+        }
+    }
 }
 
 // ---- trellis tile decode ---------------------------------------------------------------------------------------------

@@ -55,12 +55,24 @@ void set_error(const std::string& msg);
 
 // Hyper-connection epilogue of the combine (exllamav3 hc_apply as glm53/k_hcfuse.py:62-91 restates it): instead of
 // writing the layer output y, update the row's stream stack in place, x_g <- post_g * y + sum_h comb[h][g] * x_h.
+// Expert-parallel return (glmx_peer_out of glmx.h): instead of writing out, the combine stores token t's fp32 row into
+// rank t / rpr's receive buffer, slot [seq & 1][rank][t % rpr], over peer memory; the combine's last CTA then sets
+// flag [seq & 1][rank] = seq on every rank.
+struct PeerOut
+{
+    float* const* recv;    // device array [world]: each rank's float [2][world][rpr][H]
+    int* const* flags;     // device array [world]: each rank's int [2][world]
+    int* counter;          // this rank's arrival counter (zero between calls)
+    int rank, world, rpr, seq;
+};
+
 struct HcOut
 {
     float* x;              // [ntok][4][H] fp32 stream stack, updated in place
     const float* post;     // [ntok][4]
     const float* comb;     // [ntok][4][4], comb[h][g]
     int y_half;            // 1: y is rounded to fp16 first (an fp16 sublayer output), 0: fp32
+    PeerOut peer;          // peer.recv != nullptr (and x == nullptr): expert-parallel return instead of out
 };
 
 // launchers (return cudaError_t of the launch)

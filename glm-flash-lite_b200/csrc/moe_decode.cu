@@ -368,11 +368,8 @@ struct CombineArgs
     HcOut hc;                           // hc.x != nullptr: hyper-connection epilogue instead of writing out
 };
 
-__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
+__device__ __forceinline__ void combine_cols(const CombineArgs& a, int t, int c)
 {
-    const int t = blockIdx.y;
-    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (c >= a.H) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < a.topk; ++k)
     {
@@ -390,6 +387,12 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
         const int r = a.plan->P + t;
         const float4 y = *reinterpret_cast<const float4*>(a.y + (size_t) r * a.H + c);
         acc.x = __fadd_rn(acc.x, y.x); acc.y = __fadd_rn(acc.y, y.y); acc.z = __fadd_rn(acc.z, y.z); acc.w = __fadd_rn(acc.w, y.w);
+    }
+    if (a.hc.peer.recv)
+    {
+        const PeerOut& p = a.hc.peer;
+        *reinterpret_cast<float4*>(peer_row(p.recv, p.rank, p.world, p.rpr, p.seq, t, a.H) + c) = acc;
+        return;
     }
     if (a.hc.x)
     {
@@ -418,6 +421,14 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
 #pragma unroll
         for (int i = 0; i < 4; ++i) p[i] = __float2half_rn(a.accumulate ? __fadd_rn(__half2float(p[i]), v[i]) : v[i]);
     }
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
+{
+    const int t = blockIdx.y;
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (c < a.H) combine_cols(a, t, c);
+    if (a.hc.peer.recv) peer_done(a.hc.peer.recv, a.hc.peer.flags, a.hc.peer.counter, a.hc.peer.rank, a.hc.peer.world, a.hc.peer.seq);
 }
 
 // ---- known-answer decode of whole tiles (the GEMV's own decode_frag_tc, rows un-permuted on the way out) ----

@@ -457,9 +457,18 @@ struct CombineI16Args
     HcOut hc;                           // hc.x != nullptr: hyper-connection epilogue instead of writing out
 };
 
-// the combined value of token t, columns hb*128 + lane + 32q: hyper-connection update or (accumulating) store
+// the combined value of token t, columns hb*128 + lane + 32q: hyper-connection update, expert-parallel return to the
+// token's owner rank, or (accumulating) store
 __device__ __forceinline__ void combine_store(const CombineI16Args& a, int t, int hb, int lane, const float acc[4])
 {
+    if (a.hc.peer.recv)
+    {
+        const PeerOut& p = a.hc.peer;
+        float* dst = peer_row(p.recv, p.rank, p.world, p.rpr, p.seq, t, a.H) + hb * 128 + lane;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[32 * q] = acc[q];
+        return;
+    }
     if (a.hc.x)
     {
 #pragma unroll
@@ -495,10 +504,9 @@ __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int t = (int) (wid / nbk);
-    if (t >= a.ntok) return;
     const int hb = (int) (wid % nbk);
     float acc[4] = { 0.f, 0.f, 0.f, 0.f };
-    const int nk = a.topk + (a.has_shared ? 1 : 0);
+    const int nk = t < a.ntok ? a.topk + (a.has_shared ? 1 : 0) : 0;
     for (int k = 0; k < nk; ++k)
     {
         int r;
@@ -523,7 +531,8 @@ __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
             acc[q] = k < a.topk ? __fadd_rn(acc[q], __fmul_rn(w, yq)) : __fadd_rn(acc[q], yq);
         }
     }
-    combine_store(a, t, hb, lane, acc);
+    if (t < a.ntok) combine_store(a, t, hb, lane, acc);
+    if (a.hc.peer.recv) peer_done(a.hc.peer.recv, a.hc.peer.flags, a.hc.peer.counter, a.hc.peer.rank, a.hc.peer.world, a.hc.peer.seq);
 }
 
 // Small batches: one CTA per (token, 128-output block), one warp per pick computing its weighted down out_block into
@@ -569,15 +578,18 @@ __global__ void __launch_bounds__(256) combine_wide_kernel(CombineI16Args a)
         if (lane == 0) valid[k] = 1;
     }
     __syncthreads();
-    if (warp != 0) return;
-    float acc[4] = { 0.f, 0.f, 0.f, 0.f };
-    for (int k = 0; k < nk; ++k)
-        if (valid[k])
-        {
+    if (warp == 0)
+    {
+        float acc[4] = { 0.f, 0.f, 0.f, 0.f };
+        for (int k = 0; k < nk; ++k)
+            if (valid[k])
+            {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[q] = __fadd_rn(acc[q], ys[k][lane + 32 * q]);
-        }
-    combine_store(a, t, hb, lane, acc);
+                for (int q = 0; q < 4; ++q) acc[q] = __fadd_rn(acc[q], ys[k][lane + 32 * q]);
+            }
+        combine_store(a, t, hb, lane, acc);
+    }
+    if (a.hc.peer.recv) peer_done(a.hc.peer.recv, a.hc.peer.flags, a.hc.peer.counter, a.hc.peer.rank, a.hc.peer.world, a.hc.peer.seq);
 }
 
 // the combine for ntok tokens: the wide form at decode sizes, one warp per (token, block) above

@@ -28,6 +28,12 @@ class LayerDesc(C.Structure):
                 ("first_expert", _I)]
 
 
+class PeerOut(C.Structure):
+    """glmx_peer_out of include/glmx.h"""
+    _fields_ = [("recv", _P), ("flags", _P), ("counter", _P), ("rank", _I), ("world", _I), ("rows_per_rank", _I),
+                ("seq", _I)]
+
+
 class GlmxError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"glmx error {code}: {msg}")
@@ -38,7 +44,9 @@ class GlmxError(RuntimeError):
 EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_destroy", "glmx_layer_set_act_limit",
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
            "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc",
-           "glmx_selftest_bounded_wait", "glmx_router")
+           "glmx_selftest_bounded_wait", "glmx_router", "glmx_moe_forward_peer", "glmx_peer_reduce", "glmx_ep_split", "glmx_ipc_alloc",
+           "glmx_ipc_free", "glmx_ipc_handle", "glmx_ipc_open", "glmx_ipc_close")
+IPC_HANDLE_BYTES = 64
 NOALLOC_SCRATCH_BYTES = 48 << 20
 ROUTER_MAX_EXPERTS = 512
 
@@ -83,6 +91,22 @@ def load(path: str = LIB_PATH):
     L.glmx_selftest_bounded_wait.restype = _I
     L.glmx_router.argtypes = [_P, _I, _I, _I, _P, _I, _P, _I, _I, _I, _I, _I, C.c_float, _P, _P, _I, _P, _I, _P]
     L.glmx_router.restype = _I
+    L.glmx_moe_forward_peer.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, C.POINTER(PeerOut), _P, C.c_size_t, _P]
+    L.glmx_moe_forward_peer.restype = _I
+    L.glmx_peer_reduce.argtypes = [_P, _P, _I, _I, _I, _I, _P, _I, _P, _P]
+    L.glmx_peer_reduce.restype = _I
+    L.glmx_ep_split.argtypes = [_P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]
+    L.glmx_ep_split.restype = _I
+    L.glmx_ipc_alloc.argtypes = [C.c_size_t, C.POINTER(_P)]
+    L.glmx_ipc_alloc.restype = _I
+    L.glmx_ipc_free.argtypes = [_P]
+    L.glmx_ipc_free.restype = _I
+    L.glmx_ipc_handle.argtypes = [_P, _P]
+    L.glmx_ipc_handle.restype = _I
+    L.glmx_ipc_open.argtypes = [_P, C.POINTER(_P)]
+    L.glmx_ipc_open.restype = _I
+    L.glmx_ipc_close.argtypes = [_P]
+    L.glmx_ipc_close.restype = _I
     if L.glmx_version() != ABI_VERSION:
         raise RuntimeError(f"libglmx ABI {L.glmx_version()} != {ABI_VERSION}")
     _lib = L

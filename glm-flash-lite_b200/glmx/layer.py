@@ -190,6 +190,18 @@ class MoELayer:
                                            _stream_ptr(stream)))
         return hc_x
 
+    def forward_peer(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, peer: "_lib.PeerOut",
+                     mode: int = _lib.MODE_I16, stream=None) -> None:
+        """The layer with the expert-parallel return (glmx_moe_forward_peer): each token's row goes to its owner
+        rank's receive buffer instead of an output tensor (see glmx.ep)."""
+        x = x.contiguous(); sel = sel.contiguous(); w = w.contiguous()
+        ntok = x.shape[0]
+        topk = sel.shape[1] if sel.dim() == 2 else 0
+        ws = self.workspace(ntok, topk)
+        check(self.lib.glmx_moe_forward_peer(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
+                                             _dt(w), topk, int(mode), C.byref(peer), ws.data_ptr(), ws.numel(),
+                                             _stream_ptr(stream)))
+
     def check_device(self, ntok: int, topk: int, stream=None) -> int:
         """Synchronise and read the device error word of the last call (0 = fine)."""
         flags = C.c_int(0)

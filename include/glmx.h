@@ -142,6 +142,42 @@ GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* works
  * *flag (the bit glmx_check reports for a stalled forward). The kernel returns normally; the context stays usable. */
 GLMX_API int glmx_selftest_bounded_wait(int timeout_us, int* flag, void* stream);
 
+/* Expert-parallel return over peer memory. A rank of `world` holds a shard of the experts (first_expert, n_experts)
+ * and runs the layer over all ranks' gathered rows, rows_per_rank consecutive rows per rank (ntok = world *
+ * rows_per_rank). glmx_moe_forward_peer computes like glmx_moe_forward but, instead of writing `out`, its combine stores
+ * token t's fp32 row into rank (t / rows_per_rank)'s receive buffer at [seq & 1][rank][t % rows_per_rank], through the
+ * peer mappings, then sets that rank's flag [seq & 1][rank] = seq. glmx_peer_reduce, on the owner, waits for all world
+ * flags of call `seq` (bounded: on expiry it ORs 16 into *err and writes nothing) and writes out[r] = the sum of the
+ * world rows in rank order. It replaces the reduce-scatter of a plain expert-parallel layer (the reference has no
+ * multi-GPU mode). Calls of the same buffers must alternate parity (seq, seq + 1, ...), and a rank may start call seq + 2
+ * only after a collective that every owner enters after its call-seq reduce (the next call's dispatch does). */
+typedef struct glmx_peer_out {
+    void* const* recv;  /* device array [world]: rank d's receive buffer, float [2][world][rows_per_rank][hidden] */
+    int* const* flags;  /* device array [world]: rank d's flags, int [2][world], zero before the first call */
+    int* counter;       /* this rank's device int, zero before the first call (left zero after each call) */
+    int rank, world, rows_per_rank, seq;
+} glmx_peer_out;
+GLMX_API int glmx_moe_forward_peer(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
+                                   int sel_dtype, const void* w, int w_dtype, int topk, int mode, const glmx_peer_out* peer,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+GLMX_API int glmx_peer_reduce(const float* recv, const int* flags, int world, int rows_per_rank, int hidden, int seq,
+                              void* out, int out_dtype, int* err, void* stream);
+/* The shard's picks of the gathered rows, one kernel: route int32 [rows][2 * topk] = global expert ids then the fp32
+ * weights' bits; loc int32 / w fp32 [rows][topk + (shared ? 1 : 0)]: ids in [first, first + n) become 0 .. n - 1 with
+ * their weight, others -1 with weight 0; with shared, a last column of local id n (weight 1) on rows
+ * [own_begin, own_end) (the rank's own rows) and -1 elsewhere. */
+GLMX_API int glmx_ep_split(const int* route, int rows, int topk, int first, int n, int shared, int own_begin, int own_end,
+                           int* loc, float* w, void* stream);
+/* CUDA IPC for those buffers: glmx_ipc_alloc makes a zeroed device allocation of its own (the mapping in another
+ * process then starts at the buffer), glmx_ipc_handle its handle (GLMX_IPC_HANDLE_BYTES bytes), glmx_ipc_open maps a
+ * peer's handle, glmx_ipc_close / glmx_ipc_free undo them. */
+#define GLMX_IPC_HANDLE_BYTES 64
+GLMX_API int glmx_ipc_alloc(size_t bytes, void** dev_ptr);
+GLMX_API int glmx_ipc_free(void* dev_ptr);
+GLMX_API int glmx_ipc_handle(const void* dev_ptr, void* handle);
+GLMX_API int glmx_ipc_open(const void* handle, void** dev_ptr);
+GLMX_API int glmx_ipc_close(void* dev_ptr);
+
 /* Router of the MoE site, in front of the split: the GLM-4 MoE routing that exllamav3's router produces for the
  * reference's routing_fn hook (glm53/cpu_tier.py:305-335, sel [bsz, k] and w [bsz, k]). With gate_w (E x hidden,
  * row-major, dtype gate_dtype) the logits are computed first, logits[t][e] = sum_h z[t][h] * gate_w[e][h] with exact

@@ -47,3 +47,7 @@ def test_version_and_error_without_gpu():
     assert R(288, 8, 2, 80) == _lib.E_ARG                 # topk beyond the kept groups
     assert R(288, 1, 1, 8) == _lib.E_ARG and b"required" in L.glmx_last_error()   # null outputs
     assert R(288, 1, 1, 8, ntok=-1) == _lib.E_ARG
+    assert L.glmx_peer_reduce(None, None, 2, 4, 256, 1, None, _lib.F32, None, None) == _lib.E_ARG
+    assert L.glmx_ep_split(None, 4, 0, 0, 36, 1, 0, 4, None, None, None) == _lib.E_ARG       # topk 0
+    assert L.glmx_ep_split(None, 0, 8, 0, 36, 1, 0, 0, None, None, None) == _lib.OK          # nothing to do
+    assert L.glmx_moe_forward_peer(None, None, _lib.F16, 2, None, _lib.I32, None, _lib.F32, 8, 2, None, None, 0, None) == _lib.E_ARG
