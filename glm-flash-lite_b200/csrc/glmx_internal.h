@@ -33,6 +33,7 @@ struct Plan
     int S_gu;    // split-K of the gate/up kernel
     int S_d;     // split-K of the down kernel
     int ntok, topk, pad;
+    int next_gu, next_d;   // item counters of the I16 gate/up and down GEMVs (zeroed here, taken by their CTAs)
 };
 
 // Workspace layout of one forward call (byte offsets from the workspace base, 256-byte aligned).

@@ -67,6 +67,7 @@ struct GemvI16Args
     // (counters [J][ndim/128], cleared by the route kernel) runs the per-class fp32 chains in block order
     int* isum;
     int* counters;
+    int* next;                      // item counter (zeroed by the route kernel): CTAs take items as they free up
 };
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory"); }
@@ -147,13 +148,19 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
     const int kbs = nkb / S;                                                 // blocks per split
     const long long items = (long long) pl.J * nb * S;
     __shared__ int s_last;
+    // Items are taken from a global counter as CTAs free up (the co-resident CTAs of an SM progress at unequal rates,
+    // so a fixed share per CTA leaves stragglers); the producer writes each item's id into the slot of its first stage
+    // and, after the last item, an end marker (-1) in one more slot completed with a plain arrival.
+    __shared__ int s_item[C::NST];
 
     if (warp == NW)
     {
         if (lane != 0) return;
         long long it = 0;
-        for (long long item = blockIdx.x; item < items && !s_abort; item += gridDim.x)
+        for (;;)
         {
+            const long long item = s_abort ? items : (long long) atomicAdd(a.next, 1);
+            if (item >= items) break;
             const int ks = (int) (item % S);
             const long long jn = item / S;
             const int nbi = (int) (jn % nb), j = (int) (jn / nb);
@@ -167,6 +174,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                 if (!s_abort && !mbar_wait_bounded(&empty[s], ph ^ 1u)) { atomicOr(a.err, ERR_TIMEOUT_EMPTY); s_abort = 1; }
                 if (s_abort) break;
                 uint8_t* st = ring + s * C::STAGE;
+                s_item[s] = (int) item;
                 mbar_arrive_expect_tx(&full[s], (uint32_t) C::STAGE);
 #pragma unroll
                 for (int r = 0; r < RB; ++r)
@@ -186,6 +194,17 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                 }
             }
         }
+        if (!s_abort)
+        {
+            const int s = (int) (it % C::NST);
+            if (mbar_wait_bounded(&empty[s], (uint32_t) (((it / C::NST) & 1) ^ 1)))
+            {
+                s_item[s] = -1;
+                mbar_arrive(&full[s]);
+                ++it;
+            }
+            else { atomicOr(a.err, ERR_TIMEOUT_EMPTY); s_abort = 1; }
+        }
         const long long first = it > C::NST ? it - C::NST : 0;
         for (long long k = first; k < it; ++k)
             if (!mbar_wait_bounded(&full[k % C::NST], (uint32_t) ((k / C::NST) & 1))) { atomicOr(a.err, ERR_TIMEOUT_FULL); break; }
@@ -198,8 +217,17 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
     L1.init(lane);
     const int g = lane >> 2, tq = lane & 3;
     long long it = 0;
-    for (long long item = blockIdx.x; item < items; item += gridDim.x)
+    for (;;)
     {
+        // the next item: its id is in the slot of its first stage
+        {
+            const int s = (int) (it % C::NST);
+            if (!s_abort && !mbar_wait_bounded(&full[s], (uint32_t) ((it / C::NST) & 1))) { atomicOr(a.err, ERR_TIMEOUT_FULL); s_abort = 1; }
+        }
+        if (s_abort) break;
+        const int item_id = s_item[it % C::NST];
+        if (item_id < 0) break;
+        const long long item = item_id;
         const int ks = (int) (item % S);
         const long long jn = item / S;
         const int nbi = (int) (jn % nb), j = (int) (jn / nb);
@@ -214,7 +242,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
         {
             const int s = (int) (it % C::NST);
             const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
-            if (!s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(a.err, ERR_TIMEOUT_FULL); s_abort = 1; }
+            if (kb != ks * kbs && !s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(a.err, ERR_TIMEOUT_FULL); s_abort = 1; }
             const uint8_t* st = ring + s * C::STAGE;
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
@@ -700,6 +728,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         g.yraw = reinterpret_cast<float*>(ws + lay.yraw_gu);
         g.isum = rows <= I16_SPLIT_MAX_ROWS ? reinterpret_cast<int*>(ws + lay.isum_gu) : nullptr;
         g.counters = reinterpret_cast<int*>(ws + lay.cnt_gu);
+        g.next = reinterpret_cast<int*>(ws + lay.plan + offsetof(Plan, next_gu));
         switch (L.bits[0])
         {
             case 2: e = launch_gu_i16_k0<2>(L, g, st); break;
@@ -731,6 +760,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         d.yraw = reinterpret_cast<float*>(ws + lay.yrow);
         d.isum = nullptr;                       // the down GEMV has J x H/128 column blocks: enough items unsplit
         d.counters = nullptr;
+        d.next = reinterpret_cast<int*>(ws + lay.plan + offsetof(Plan, next_d));
         switch (L.bits[2])
         {
             case 2: e = launch_gemv_i16<2, 2, 1>(L, d, st); break;

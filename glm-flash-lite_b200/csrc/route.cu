@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
         pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_slots);
         pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_slots);
         pl.ntok = a.ntok; pl.topk = a.topk; pl.pad = 0;
+        pl.next_gu = 0; pl.next_d = 0;
         *a.plan = pl;
         *a.err = 0;
     }
