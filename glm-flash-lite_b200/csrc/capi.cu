@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "glmx_common.cuh"
 #include "glmx_internal.h"
@@ -79,6 +80,24 @@ int glmx_layer_create(const glmx_layer_desc* d, glmx_layer** out)
     if (e != cudaSuccess) { delete l; return cuda_fail(e, "glmx_layer_create: cudaMalloc"); }
     e = cudaMemcpy(L.d_trellis, d->trellis, sizeof(uint64_t) * et * 3, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { cudaFree(L.d_trellis); delete l; return cuda_fail(e, "glmx_layer_create: cudaMemcpy"); }
+    // the GEMV kernels' tensor maps, one per (expert, projection)
+    {
+        std::vector<CUtensorMap> maps((size_t) et * 3);
+        for (int i = 0; i < et * 3 && e == cudaSuccess; ++i)
+        {
+            const int p = i % 3;
+            e = trellis_map(&maps[i], reinterpret_cast<const void*>(d->trellis[i]), p < 2 ? L.H : L.I, p < 2 ? L.I : L.H, L.bits[p]);
+        }
+        if (e == cudaSuccess) e = cudaMalloc(&L.d_tmaps, sizeof(CUtensorMap) * maps.size());
+        if (e == cudaSuccess) e = cudaMemcpy(L.d_tmaps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess)
+        {
+            if (L.d_tmaps) cudaFree(L.d_tmaps);
+            cudaFree(L.d_trellis);
+            delete l;
+            return cuda_fail(e, "glmx_layer_create: trellis tensor maps");
+        }
+    }
     *out = l;
     return GLMX_OK;
 }
@@ -87,6 +106,7 @@ int glmx_layer_destroy(glmx_layer* l)
 {
     if (!l) return GLMX_OK;
     if (l->L.d_trellis) cudaFree(l->L.d_trellis);
+    if (l->L.d_tmaps) cudaFree(l->L.d_tmaps);
     delete l;
     return GLMX_OK;
 }

@@ -7,6 +7,7 @@
 //   Stream weights 8t..8t+7 sit at the tile positions the mma.m16n8k16 A fragment gives lane t when A = W^T
 //   (PERM, ft_core.h:48-61), so one lane decodes exactly its own fragment.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -79,6 +80,17 @@ __device__ __forceinline__ bool mbar_wait_bounded_ns(uint64_t* bar, uint32_t par
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity)
 {
     return mbar_wait_bounded_ns(bar, parity, (uint64_t) WAIT_TIMEOUT_NS);
+}
+
+// 2-D tiled tensor copy global -> shared (the innermost coordinate x times the element size a multiple of 16 bytes),
+// completion counted on `bar`
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes and addresses 16-byte aligned)

@@ -1,5 +1,6 @@
 // Internal (non-ABI) declarations shared by the .cu files of libglmx.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -22,7 +23,11 @@ struct Layer
     uint64_t* d_trellis = nullptr;     // device [E_total][3] addresses (gate, up, down)
     const uint16_t* suh[3] = {};       // device fp16 [E_total][k]
     const uint16_t* svh[3] = {};       // device fp16 [E_total][n]
+    CUtensorMap* d_tmaps = nullptr;    // device [E_total][3] tensor maps of the trellis tensors (GEMV stage boxes)
 };
+
+// tensor map of one trellis tensor [k x n] at `base` for the GEMV kernels (boxes of 8 k-tile rows x 8 tiles)
+cudaError_t trellis_map(CUtensorMap* m, const void* base, int k, int n, int bits);
 
 // Per-call routing plan, written by the route kernel and read by the later kernels.
 struct Plan

@@ -44,10 +44,11 @@ struct CfgI
     static constexpr int MAT0 = RB * ROW0, MAT1 = NMAT > 1 ? RB * ROW1 : 0;
     static constexpr int ACT = NMAT * I16_ACT_BYTES;
     static constexpr int SC = NMAT * 16;
-    static constexpr int STAGE = MAT0 + MAT1 + ACT + SC;
+    static constexpr int BYTES = MAT0 + MAT1 + ACT + SC;                  // bytes copied into a stage
+    static constexpr int STAGE = (BYTES + 127) / 128 * 128;                 // tensor copies land 128-byte aligned
     static constexpr int NST = RING / STAGE < 2 ? 2 : (RING / STAGE > 8 ? 8 : RING / STAGE);
     static constexpr int SMEM = NST * STAGE + 2 * NST * 8;
-    static_assert(STAGE % 16 == 0, "stage alignment");
+    static_assert(STAGE % 128 == 0 && MAT0 % 128 == 0 && (MAT0 + MAT1) % 16 == 0, "stage alignment");
 };
 
 struct GemvI16Args
@@ -55,6 +56,7 @@ struct GemvI16Args
     const Plan* plan;
     const int4* jobs;
     const uint64_t* trellis;
+    const CUtensorMap* tmaps;       // [E_total][3]: each trellis tensor as rows of k-tiles (boxes of 8 rows x 8 tiles)
     int proj0, nmat;
     int kt, ntn, ndim;              // k-tiles, n-tiles, output dim
     const uint8_t* actb;            // [J][nmat][kt/8][I16_ACT_BYTES]
@@ -165,8 +167,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
             const long long jn = item / S;
             const int nbi = (int) (jn % nb), j = (int) (jn / nb);
             const int4 job = a.jobs[j];
-            const uint8_t* b0 = reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0]);
-            const uint8_t* b1 = NMAT > 1 ? reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0 + 1]) : nullptr;
+            const CUtensorMap* m0 = a.tmaps + job.x * 3 + a.proj0;
             for (int kb = ks * kbs; kb < (ks + 1) * kbs; ++kb, ++it)
             {
                 const int s = (int) (it % C::NST);
@@ -175,16 +176,10 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                 if (s_abort) break;
                 uint8_t* st = ring + s * C::STAGE;
                 s_item[s] = (int) item;
-                mbar_arrive_expect_tx(&full[s], (uint32_t) C::STAGE);
-#pragma unroll
-                for (int r = 0; r < RB; ++r)
-                    bulk_g2s(st + r * C::ROW0, b0 + ((size_t) (kb * RB + r) * a.ntn + nbi * NW) * C::TB0, C::ROW0, &full[s]);
-                if (NMAT > 1)
-                {
-#pragma unroll
-                    for (int r = 0; r < RB; ++r)
-                        bulk_g2s(st + C::MAT0 + r * C::ROW1, b1 + ((size_t) (kb * RB + r) * a.ntn + nbi * NW) * C::TB1, C::ROW1, &full[s]);
-                }
+                mbar_arrive_expect_tx(&full[s], (uint32_t) C::BYTES);
+                // the stage's RB k-tile rows x NW tiles of each matrix: one tensor copy (x in 32-bit words)
+                tma_load_2d(st, m0, nbi * NW * C::TB0 / 4, kb * RB, &full[s]);
+                if (NMAT > 1) tma_load_2d(st + C::MAT0, m0 + 1, nbi * NW * C::TB1 / 4, kb * RB, &full[s]);
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
                 {
@@ -720,7 +715,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         if ((e = mark(2)) != cudaSuccess) return e;
 
         GemvI16Args g;
-        g.plan = plan; g.jobs = jobs; g.trellis = L.d_trellis; g.err = reinterpret_cast<int*>(ws + lay.err);
+        g.plan = plan; g.jobs = jobs; g.trellis = L.d_trellis; g.tmaps = L.d_tmaps; g.err = reinterpret_cast<int*>(ws + lay.err);
         g.proj0 = 0; g.nmat = 2; g.kt = L.H / 16; g.ntn = L.I / 16; g.ndim = L.I;
         g.actb = ws + lay.actb_gu;
         g.scales = reinterpret_cast<const float*>(ws + lay.sc_gu);

@@ -122,14 +122,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // four 8x8 b16 matrices (the registers of an m16n8k16 A fragment) to shared memory, one 16-byte row per lane address
 __device__ __forceinline__ void stmatrix_x4(uint32_t saddr, const uint32_t a[4])
@@ -483,6 +475,27 @@ cudaError_t act_map(CUtensorMap* m, const void* base, int kdim, int rows)
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
+
+}  // namespace
+
+// The GEMV kernels' view of one trellis tensor [k x n]: rows of k-tiles, each ntn tiles of 32 * bits bytes, as 32-bit
+// words; boxes of 8 consecutive k-tile rows x 8 tiles (one stage of one 128-column item).
+cudaError_t trellis_map(CUtensorMap* m, const void* base, int k, int n, int bits)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const int tb = 32 * bits, ntn = n / 16, kt = k / 16;
+    const cuuint64_t dims[2] = { (cuuint64_t) ntn * tb / 4, (cuuint64_t) kt };
+    const cuuint64_t strides[1] = { (cuuint64_t) ntn * tb };
+    const cuuint32_t box[2] = { (cuuint32_t) (8 * tb / 4), 8u };
+    const cuuint32_t es[2] = { 1, 1 };
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+namespace {
 
 template <int K, int TN>
 cudaError_t launch_gemm_pf(const Layer& L, const CUtensorMap& m0, const CUtensorMap& m1, const PfArgs& a, long long max_tiles,
