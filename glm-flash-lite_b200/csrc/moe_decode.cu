@@ -43,11 +43,11 @@ struct Cfg
     static constexpr int ROW0 = 8 * TB0, ROW1 = 8 * TB1;
     static constexpr int MAT0 = RB * ROW0, MAT1 = NMAT > 1 ? RB * ROW1 : 0;
     static constexpr int XS = MAXM * XROW;
-    static constexpr int STAGE = MAT0 + MAT1 + NMAT * XS;
+    static constexpr int STAGE = (MAT0 + MAT1 + NMAT * XS + 127) / 128 * 128;   // tensor copies land 128-byte aligned
     static constexpr int NST = RING_BYTES / STAGE < 3 ? 3 : (RING_BYTES / STAGE > 12 ? 12 : RING_BYTES / STAGE);
     static constexpr int RED = NMAT * MAXM * 128 * 4;
     static constexpr int SMEM = NST * STAGE + RED + 2 * NST * 8;
-    static_assert(STAGE % 16 == 0, "stage alignment");
+    static_assert(STAGE % 128 == 0 && MAT0 % 128 == 0 && (MAT0 + MAT1) % 16 == 0, "stage alignment");
 };
 
 struct GemvArgs
@@ -55,6 +55,7 @@ struct GemvArgs
     const Plan* plan;
     const int4* jobs;
     const uint64_t* trellis;     // [E_total][3]
+    const CUtensorMap* tmaps;    // [E_total][3]: each trellis tensor as rows of k-tiles (boxes of 8 rows x 8 tiles)
     int proj0;                   // projection index of matrix 0 (0 = gate, 2 = down)
     int kt, ntn;                 // k-tiles and n-tiles of the matrix
     int kdim, ndim;              // K and N
@@ -109,8 +110,7 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
             const long long jn = item / S;
             const int nbi = (int) (jn % nb), j = (int) (jn / nb);
             const int4 job = a.jobs[j];
-            const uint8_t* b0 = reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0]);
-            const uint8_t* b1 = NMAT > 1 ? reinterpret_cast<const uint8_t*>(a.trellis[job.x * 3 + a.proj0 + 1]) : nullptr;
+            const CUtensorMap* m0 = a.tmaps + job.x * 3 + a.proj0;
             const uint32_t bytes = (uint32_t) (C::MAT0 + C::MAT1 + NMAT * job.z * 256);
             for (int q = 0; q < kqs; ++q, ++it)
             {
@@ -121,15 +121,9 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
                 const int kr = (ks * kqs + q) * RB;
                 uint8_t* st = ring + s * C::STAGE;
                 mbar_arrive_expect_tx(&full[s], bytes);
-#pragma unroll
-                for (int r = 0; r < RB; ++r)
-                    bulk_g2s(st + r * C::ROW0, b0 + ((size_t) (kr + r) * a.ntn + nbi * 8) * C::TB0, C::ROW0, &full[s]);
-                if (NMAT > 1)
-                {
-#pragma unroll
-                    for (int r = 0; r < RB; ++r)
-                        bulk_g2s(st + C::MAT0 + r * C::ROW1, b1 + ((size_t) (kr + r) * a.ntn + nbi * 8) * C::TB1, C::ROW1, &full[s]);
-                }
+                // the stage's RB k-tile rows x 8 tiles of each matrix: one tensor copy (x in 32-bit words)
+                tma_load_2d(st, m0, nbi * 8 * C::TB0 / 4, kr, &full[s]);
+                if (NMAT > 1) tma_load_2d(st + C::MAT0, m0 + 1, nbi * 8 * C::TB1 / 4, kr, &full[s]);
                 uint8_t* xs = st + C::MAT0 + C::MAT1;
                 for (int i = 0; i < job.z; ++i)
                     bulk_g2s(xs + i * XROW, a.xin0 + (size_t) (job.y + i) * a.kdim + kr * 16, 256, &full[s]);
@@ -605,6 +599,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
         g.plan = plan;
         g.jobs = reinterpret_cast<const int4*>(ws + lay.jobs);
         g.trellis = L.d_trellis;
+        g.tmaps = L.d_tmaps;
         g.err = reinterpret_cast<int*>(ws + lay.err);
         g.partials = reinterpret_cast<float*>(ws + lay.partials);
         g.act_limit = L.act_limit;
