@@ -47,7 +47,7 @@ struct WsLayout
     size_t plan, err, offsets, row_token, row_expert, row_pick, row_weight, pick_row, jobs, row_job;
     size_t cnt_gu, cnt_d, xg, xu, xd, yrow, partials;
     // I16 mode
-    size_t actb_gu, sc_gu, psum_gu, yraw_gu, actb_d, sc_d, psum_d, isum_gu;
+    size_t actb_gu, psum_gu, yraw_gu, actb_d, psum_d, isum_gu;
     size_t total;
     int rows_max, jobs_max, jobs_max_i16, part_slots;
 };
@@ -105,6 +105,9 @@ cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int 
 
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
+// one (job, 128-input block) record of the I16 activations, laid out as a GEMV stage holds it: the nmat projections'
+// planes, then their 4 scales (16 bytes each)
+__host__ __device__ constexpr size_t i16_rec_bytes(int nmat) { return (size_t) nmat * (I16_ACT_BYTES + 16); }
 constexpr int I16_MAX_ROWS = 8192;     // I16 is the decode mode: its activation layout is sized for up to this many rows
 constexpr int I16_SPLIT_MAX_ROWS = 16; // calls this small split the I16 gate/up GEMV along K (exact int32 block sums)
 constexpr int PF_MAXM = 128;           // rows per job of the prefill GEMM (one tensor-core tile)

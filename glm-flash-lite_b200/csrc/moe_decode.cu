@@ -547,11 +547,9 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     const int ji = rows <= I16_MAX_ROWS ? (rows < (rows + 3) / 4 + L.E_total ? rows : (rows + 3) / 4 + L.E_total) : 0;
     w.jobs_max_i16 = ji;
     const int BH = L.H / 128, BI = L.I / 128;
-    w.actb_gu = take((size_t) ji * 2 * BH * I16_ACT_BYTES);
-    w.sc_gu = take(sizeof(float) * 4 * (size_t) ji * 2 * BH);
+    w.actb_gu = take((size_t) ji * BH * i16_rec_bytes(2));
     w.psum_gu = take(sizeof(float) * (size_t) (ji ? rows : 0) * 2 * BH);
-    w.actb_d = take((size_t) ji * BI * I16_ACT_BYTES);
-    w.sc_d = take(sizeof(float) * 4 * (size_t) ji * BI);
+    w.actb_d = take((size_t) ji * BI * i16_rec_bytes(1));
     w.psum_d = take(sizeof(float) * (size_t) (ji ? rows : 0) * BI);
     // K-split class sums of the I16 gate/up GEMV for calls of at most I16_SPLIT_MAX_ROWS rows
     w.isum_gu = take(ji && rows <= I16_SPLIT_MAX_ROWS ? sizeof(int) * 4 * (size_t) rows * 2 * BH * L.I : 0);

@@ -59,8 +59,7 @@ struct GemvI16Args
     const CUtensorMap* tmaps;       // [E_total][3]: each trellis tensor as rows of k-tiles (boxes of 8 rows x 8 tiles)
     int proj0, nmat;
     int kt, ntn, ndim;              // k-tiles, n-tiles, output dim
-    const uint8_t* actb;            // [J][nmat][kt/8][I16_ACT_BYTES]
-    const float* scales;            // [J][nmat][kt/8][4]
+    const uint8_t* actb;            // [J][kt/8] records of i16_rec_bytes(nmat): planes of each projection, then scales
     const float* psum;              // [R][nmat][kt/8]
     float* yraw;                    // [R][nmat][ndim]
     int* err;
@@ -103,7 +102,8 @@ __device__ __noinline__ void i16_chain_item(const GemvI16Args& a, int4 job, int 
         const int slot = idx / (nmat * 128), m = (idx / 128) % nmat, col = nbi * 128 + idx % 128;
         const int row = job.y + slot;
         const int4* src = reinterpret_cast<const int4*>(a.isum) + (((size_t) row * nmat + m) * nkb) * a.ndim + col;
-        const float* scl = a.scales + ((size_t) j * nmat + m) * nkb * 4 + slot;
+        const size_t rec = i16_rec_bytes(nmat);
+        const float* scl = reinterpret_cast<const float*>(a.actb + (size_t) j * nkb * rec + nmat * I16_ACT_BYTES) + m * 4 + slot;
         float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
         for (int kb0 = 0; kb0 < nkb; kb0 += 4)
         {
@@ -111,7 +111,7 @@ __device__ __noinline__ void i16_chain_item(const GemvI16Args& a, int4 job, int 
             float sc[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-                if (kb0 + u < nkb) { v[u] = __ldcg(src + (size_t) (kb0 + u) * a.ndim); sc[u] = __ldg(scl + (kb0 + u) * 4); }
+                if (kb0 + u < nkb) { v[u] = __ldcg(src + (size_t) (kb0 + u) * a.ndim); sc[u] = __ldg(scl + (kb0 + u) * (rec / 4)); }
 #pragma unroll
             for (int u = 0; u < 4; ++u)
                 if (kb0 + u < nkb)
@@ -180,13 +180,8 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                 // the stage's RB k-tile rows x NW tiles of each matrix: one tensor copy (x in 32-bit words)
                 tma_load_2d(st, m0, nbi * NW * C::TB0 / 4, kb * RB, &full[s]);
                 if (NMAT > 1) tma_load_2d(st + C::MAT0, m0 + 1, nbi * NW * C::TB1 / 4, kb * RB, &full[s]);
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-                {
-                    const size_t blk = ((size_t) j * NMAT + m) * nkb + kb;
-                    bulk_g2s(st + C::MAT0 + C::MAT1 + m * I16_ACT_BYTES, a.actb + blk * I16_ACT_BYTES, I16_ACT_BYTES, &full[s]);
-                    bulk_g2s(st + C::MAT0 + C::MAT1 + C::ACT + m * 16, a.scales + blk * 4, 16, &full[s]);
-                }
+                // the block's activation record (every projection's planes, then their scales): one copy
+                bulk_g2s(st + C::MAT0 + C::MAT1, a.actb + ((size_t) j * nkb + kb) * (C::ACT + C::SC), C::ACT + C::SC, &full[s]);
             }
         }
         if (!s_abort)
@@ -387,7 +382,7 @@ struct PrepI16Args
     const void* x; int x_dtype; int H;
     const int* row_token; const int* row_expert; const int* row_job; const int4* jobs;
     const __half* suh_g; const __half* suh_u;
-    uint8_t* actb; float* scales; float* psum;
+    uint8_t* actb; float* psum;
 };
 
 __device__ __forceinline__ float load_x(const void* x, int dt, size_t i)
@@ -418,8 +413,9 @@ __global__ void __launch_bounds__(256) prep_i16_kernel(PrepI16Args a)
     had128_warp(v, lane);
 #pragma unroll
     for (int q = 0; q < 4; ++q) v[q] = r16(__fmul_rn(v[q], HAD));
-    const size_t blk = ((size_t) j * 2 + proj) * nbk + kb;
-    quantise_block(v, lane, slot, a.actb + blk * I16_ACT_BYTES, a.scales + blk * 4 + slot, a.psum + ((size_t) row * 2 + proj) * nbk + kb);
+    uint8_t* rec = a.actb + ((size_t) j * nbk + kb) * i16_rec_bytes(2);
+    quantise_block(v, lane, slot, rec + proj * I16_ACT_BYTES, reinterpret_cast<float*>(rec + 2 * I16_ACT_BYTES) + proj * 4 + slot,
+                   a.psum + ((size_t) row * 2 + proj) * nbk + kb);
 }
 
 struct EpiGuArgs
@@ -430,7 +426,7 @@ struct EpiGuArgs
     const float* yraw;                  // [R][2][I]
     const __half* svh_g; const __half* svh_u; const __half* suh_d;
     float act_limit;
-    uint8_t* actb; float* scales; float* psum;    // down input: [J][1][I/128]...
+    uint8_t* actb; float* psum;                  // down input: records [J][I/128] of i16_rec_bytes(1)
 };
 
 __global__ void __launch_bounds__(256) epi_gu_i16_kernel(EpiGuArgs a)
@@ -465,8 +461,8 @@ __global__ void __launch_bounds__(256) epi_gu_i16_kernel(EpiGuArgs a)
     had128_warp(av, lane);
 #pragma unroll
     for (int q = 0; q < 4; ++q) av[q] = r16(__fmul_rn(av[q], HAD));
-    const size_t blk = (size_t) j * nbk + nb;
-    quantise_block(av, lane, slot, a.actb + blk * I16_ACT_BYTES, a.scales + blk * 4 + slot, a.psum + (size_t) row * nbk + nb);
+    uint8_t* rec = a.actb + ((size_t) j * nbk + nb) * i16_rec_bytes(1);
+    quantise_block(av, lane, slot, rec, reinterpret_cast<float*>(rec + I16_ACT_BYTES) + slot, a.psum + (size_t) row * nbk + nb);
 }
 
 struct CombineI16Args
@@ -707,7 +703,6 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         p.suh_g = reinterpret_cast<const __half*>(L.suh[0]);
         p.suh_u = reinterpret_cast<const __half*>(L.suh[1]);
         p.actb = ws + lay.actb_gu;
-        p.scales = reinterpret_cast<float*>(ws + lay.sc_gu);
         p.psum = reinterpret_cast<float*>(ws + lay.psum_gu);
         const long long w1 = (long long) rows * 2 * (L.H / 128);
         prep_i16_kernel<<<(unsigned) ((w1 + 7) / 8), 256, 0, st>>>(p);
@@ -718,7 +713,6 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         g.plan = plan; g.jobs = jobs; g.trellis = L.d_trellis; g.tmaps = L.d_tmaps; g.err = reinterpret_cast<int*>(ws + lay.err);
         g.proj0 = 0; g.nmat = 2; g.kt = L.H / 16; g.ntn = L.I / 16; g.ndim = L.I;
         g.actb = ws + lay.actb_gu;
-        g.scales = reinterpret_cast<const float*>(ws + lay.sc_gu);
         g.psum = reinterpret_cast<const float*>(ws + lay.psum_gu);
         g.yraw = reinterpret_cast<float*>(ws + lay.yraw_gu);
         g.isum = rows <= I16_SPLIT_MAX_ROWS ? reinterpret_cast<int*>(ws + lay.isum_gu) : nullptr;
@@ -740,7 +734,6 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         q.suh_d = reinterpret_cast<const __half*>(L.suh[2]);
         q.act_limit = L.act_limit;
         q.actb = ws + lay.actb_d;
-        q.scales = reinterpret_cast<float*>(ws + lay.sc_d);
         q.psum = reinterpret_cast<float*>(ws + lay.psum_d);
         const long long w2 = (long long) rows * (L.I / 128);
         epi_gu_i16_kernel<<<(unsigned) ((w2 + 7) / 8), 256, 0, st>>>(q);
@@ -750,7 +743,6 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         GemvI16Args d = g;
         d.proj0 = 2; d.nmat = 1; d.kt = L.I / 16; d.ntn = L.H / 16; d.ndim = L.H;
         d.actb = ws + lay.actb_d;
-        d.scales = reinterpret_cast<const float*>(ws + lay.sc_d);
         d.psum = reinterpret_cast<const float*>(ws + lay.psum_d);
         d.yraw = reinterpret_cast<float*>(ws + lay.yrow);
         d.isum = nullptr;                       // the down GEMV has J x H/128 column blocks: enough items unsplit
