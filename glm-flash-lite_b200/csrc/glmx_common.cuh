@@ -101,6 +101,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// ---- programmatic dependent launch -----------------------------------------------------------------------------------
+// Kernels of a layer call launched with launch_chained start with pdl_enter(): wait until the previous kernel of the
+// stream has completed and its memory is visible (a no-op without a chained launch), then allow the next kernel to be
+// launched while this one runs (its CTAs are placed as resources free up and wait in their own pdl_enter()).
+__device__ __forceinline__ void pdl_enter()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
 // ---- expert-parallel return over peer memory ------------------------------------------------------------------------
 
 __device__ __forceinline__ void st_release_sys(int* p, int v)

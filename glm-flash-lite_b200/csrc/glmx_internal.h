@@ -81,6 +81,24 @@ struct HcOut
     PeerOut peer;          // peer.recv != nullptr (and x == nullptr): expert-parallel return instead of out
 };
 
+// A kernel launch that may overlap the previous kernel of the stream (programmatic dependent launch); the kernel must
+// begin with pdl_enter().
+template <typename... P, typename... A>
+cudaError_t launch_chained(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
                          int maxm, uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);

@@ -129,6 +129,7 @@ __device__ __noinline__ void i16_chain_item(const GemvI16Args& a, int4 job, int 
 template <int K0, int K1, int NMAT, bool SPLIT>
 __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
 {
+    pdl_enter();
     using C = CfgI<K0, K1, NMAT>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;
@@ -394,6 +395,7 @@ __device__ __forceinline__ float load_x(const void* x, int dt, size_t i)
 
 __global__ void __launch_bounds__(256) prep_i16_kernel(PrepI16Args a)
 {
+    pdl_enter();
     const int nbk = a.H / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -431,6 +433,7 @@ struct EpiGuArgs
 
 __global__ void __launch_bounds__(256) epi_gu_i16_kernel(EpiGuArgs a)
 {
+    pdl_enter();
     const int nbk = a.I / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -519,6 +522,7 @@ __device__ __forceinline__ void combine_store(const CombineI16Args& a, int t, in
 // one warp per (token, 128-output block): down out_block per pick, weighted sum in pick order (+ shared)
 __global__ void __launch_bounds__(256) combine_i16_kernel(CombineI16Args a)
 {
+    pdl_enter();
     const int nbk = a.H / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -561,6 +565,7 @@ constexpr int COMBINE_MAXK = 65;           // topk <= 64, plus the shared expert
 constexpr int COMBINE_WIDE_MAX_TOKENS = 32;
 __global__ void __launch_bounds__(256) combine_wide_kernel(CombineI16Args a)
 {
+    pdl_enter();
     __shared__ float ys[COMBINE_MAXK][128];
     __shared__ int valid[COMBINE_MAXK];
     const int nbk = a.H / 128;
@@ -615,13 +620,12 @@ __global__ void __launch_bounds__(256) combine_wide_kernel(CombineI16Args a)
 cudaError_t launch_combine(const CombineI16Args& c, int ntok, int H, cudaStream_t st)
 {
     if (ntok <= COMBINE_WIDE_MAX_TOKENS)
-        combine_wide_kernel<<<(unsigned) (ntok * (H / 128)), 256, 0, st>>>(c);
+        return launch_chained(combine_wide_kernel, dim3((unsigned) (ntok * (H / 128))), dim3(256), 0, st, c);
     else
     {
         const long long w3 = (long long) ntok * (H / 128);
-        combine_i16_kernel<<<(unsigned) ((w3 + 7) / 8), 256, 0, st>>>(c);
+        return launch_chained(combine_i16_kernel, dim3((unsigned) ((w3 + 7) / 8)), dim3(256), 0, st, c);
     }
-    return cudaGetLastError();
 }
 
 template <int K0, int K1, int NMAT, bool SPLIT>
@@ -638,8 +642,7 @@ cudaError_t launch_gemv_i16_v(const Layer& L, const GemvI16Args& a, cudaStream_t
             sms[L.device] = 148;
         attr_set[L.device] = true;
     }
-    gemv_i16_kernel<K0, K1, NMAT, SPLIT><<<sms[L.device] * CTAS, NTHR, C::SMEM, st>>>(a);
-    return cudaGetLastError();
+    return launch_chained(gemv_i16_kernel<K0, K1, NMAT, SPLIT>, dim3(sms[L.device] * CTAS), dim3(NTHR), C::SMEM, st, a);
 }
 
 // the K-split form only where its sums buffer exists (gate/up of calls with at most I16_SPLIT_MAX_ROWS rows)
@@ -705,8 +708,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         p.actb = ws + lay.actb_gu;
         p.psum = reinterpret_cast<float*>(ws + lay.psum_gu);
         const long long w1 = (long long) rows * 2 * (L.H / 128);
-        prep_i16_kernel<<<(unsigned) ((w1 + 7) / 8), 256, 0, st>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_chained(prep_i16_kernel, dim3((unsigned) ((w1 + 7) / 8)), dim3(256), 0, st, p)) != cudaSuccess) return e;
         if ((e = mark(2)) != cudaSuccess) return e;
 
         GemvI16Args g;
@@ -736,8 +738,7 @@ cudaError_t launch_i16_forward(const Layer& L, const void* x, int x_dtype, int n
         q.actb = ws + lay.actb_d;
         q.psum = reinterpret_cast<float*>(ws + lay.psum_d);
         const long long w2 = (long long) rows * (L.I / 128);
-        epi_gu_i16_kernel<<<(unsigned) ((w2 + 7) / 8), 256, 0, st>>>(q);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_chained(epi_gu_i16_kernel, dim3((unsigned) ((w2 + 7) / 8)), dim3(256), 0, st, q)) != cudaSuccess) return e;
         if ((e = mark(3)) != cudaSuccess) return e;
 
         GemvI16Args d = g;

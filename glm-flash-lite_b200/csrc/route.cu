@@ -107,6 +107,7 @@ __device__ int pick_split(long long units, int stages, int target, int slots)
 
 __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
 {
+    pdl_enter();
     extern __shared__ int sm[];
     const int E = a.E;
     int* cnt = sm;                                   // [E]
@@ -244,8 +245,7 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
         if (e != cudaSuccess) return e;
         attr_set[L.device] = true;
     }
-    route_kernel<<<1, RT, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_chained(route_kernel, dim3(1), dim3(RT), smem, st, a);
 }
 
 }  // namespace glmx
