@@ -154,12 +154,14 @@ __device__ __forceinline__ void peer_done(float* const* recv, int* const* flags,
 // ---- trellis tile decode ---------------------------------------------------------------------------------------------
 
 // Per-lane constants for decoding lane `lane`'s 8 stream weights of a K-bit tile: the two 32-bit words holding its
-// (7K+16)-bit window, a right pre-shift that brings every state's shift below 32, and the 8 state shifts.
+// (7K+16)-bit window and the right shift `pre` of (hi:lo) that brings the window to bits [0, 7K+16). State j then sits
+// at the compile-time shift K * (7 - j), so no per-state shift is held in registers. pre is in [0, 32] for the tile
+// layouts of K = 2, 3, 4 (K = 2 lanes whose window lies wholly in the hi word need 32).
 template <int K>
 struct LaneDecode
 {
+    static_assert(K >= 2 && K <= 4, "trellis bitrates 2..4");
     uint32_t off_hi, off_lo, pre;
-    uint32_t sh[8];
     __device__ __forceinline__ void init(int lane)
     {
         constexpr int bits = 256 * K, words = 8 * K;
@@ -167,10 +169,7 @@ struct LaneDecode
         const int wa = start / 32, rs = start % 32;
         off_hi = 4u * wa;
         off_lo = 4u * ((wa + 1) % words);
-        const int shift0 = 48 - rs;                                   // shift of state 0 in (hi:lo)
-        pre = shift0 > 31 ? shift0 - 31 : 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sh[j] = uint32_t(shift0 - (int) pre - K * j);
+        pre = uint32_t(48 - rs - 7 * K);                              // state 0 starts at bit 48 - rs of (hi:lo)
     }
 };
 
@@ -224,27 +223,29 @@ struct OnesFrag
     }
 };
 
-// The 8 product words x_j = state_j * MUL1 (mod 2^32) of lane's stream weights 8*lane .. 8*lane+7 of a tile; the
-// codebook value of weight j is a function of bytesum(x_j) (ft_core.h:75-83).
-template <int K>
-__device__ __forceinline__ void decode_words(const uint8_t* tile, const LaneDecode<K>& L, uint32_t x[8])
-{
-    const uint32_t hi = lds32(tile + L.off_hi), lo = lds32(tile + L.off_lo);
-    const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
-    const uint32_t hi2 = hi >> L.pre;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
-}
-
-// decode_words from the lane's two stream words already loaded (hi = word at off_hi, lo = word at off_lo), so a
-// caller can issue the shared-memory loads of several tiles before any of their arithmetic
+// The 8 product words x_j = state_j * MUL1 (mod 2^32) of a lane's stream weights from its two stream words (hi = word at
+// off_hi, lo = word at off_lo); the codebook value of weight j is a function of bytesum(x_j) (ft_core.h:75-83). The
+// window is first shifted to bit 0 (clamped funnel shifts: pre may be 32); states that lie in the low word then need
+// a plain shift (none for j = 7), the others a funnel shift.
 template <int K>
 __device__ __forceinline__ void decode_words_from(uint32_t hi, uint32_t lo, const LaneDecode<K>& L, uint32_t x[8])
 {
-    const uint32_t lo2 = __funnelshift_r(lo, hi, L.pre);
-    const uint32_t hi2 = hi >> L.pre;
+    const uint32_t lo2 = __funnelshift_rc(lo, hi, L.pre);
+    const uint32_t hi2 = __funnelshift_rc(hi, 0u, L.pre);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = (__funnelshift_r(lo2, hi2, L.sh[j]) & 0xffffu) * MUL1;
+    for (int j = 0; j < 8; ++j)
+    {
+        const int sh = K * (7 - j);
+        const uint32_t st = sh == 0 ? lo2 : (sh + 16 <= 32 ? lo2 >> sh : __funnelshift_r(lo2, hi2, sh));
+        x[j] = (st & 0xffffu) * MUL1;
+    }
+}
+
+// decode_words_from reading the lane's two words of the tile at `tile` (shared memory)
+template <int K>
+__device__ __forceinline__ void decode_words(const uint8_t* tile, const LaneDecode<K>& L, uint32_t x[8])
+{
+    decode_words_from<K>(lds32(tile + L.off_hi), lds32(tile + L.off_lo), L, x);
 }
 
 // mma.m16n8k32, A = product bytes (u8), B = activation planes (s8), exact int32 accumulation
