@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                         imma_u8s8(acc[c], xa[c], xa[c + 4], xb[c], xb[c + 4], bb.x, bb.y);
                     }
                 }
-                if (SPLIT && S > 1)
+                if (SPLIT)      // also for S = 1: one epilogue form per variant keeps the split variant's registers low
                 {
                     // exact class sums of this block for row slot tq, columns g and g + 8 of the warp's n-tile
                     if (tq < job.z)
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        if (SPLIT && S > 1)
+        if (SPLIT)
         {
             // the last split of this (job, column block) to arrive chains every block's sums, in block order
             __threadfence();
