@@ -219,7 +219,9 @@ static int forward_impl(const glmx_layer* l, const void* x, int x_dtype, int nto
     cudaError_t e = cudaSuccess;
     if (events && events[0]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[0]), st);
     const int maxm = base == GLMX_MODE_I16 ? I16_MAXM : gemm ? PF_MAXM : MAXM;
-    if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, maxm, wsb, lay, grid, st);
+    // the K-split plan is made for the grid of the GEMV that follows
+    const int plan_grid = base == GLMX_MODE_I16 ? i16_grid_ctas(l->L) : grid;
+    if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, maxm, wsb, lay, plan_grid, st);
     if (e == cudaSuccess && events && events[1]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[1]), st);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: route launch");
     if (base == GLMX_MODE_I16)

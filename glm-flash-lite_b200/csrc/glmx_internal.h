@@ -55,7 +55,9 @@ struct WsLayout
 WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas);
 
 // grid size of the persistent GEMV kernels on the current device
-int gemv_grid_ctas(const Layer& L);
+int gemv_grid_ctas(const Layer& L);   // resident CTAs of the EXACT GEMV grid
+int gemv_sm_count(const Layer& L);
+int i16_grid_ctas(const Layer& L);    // resident CTAs of the I16 GEMV grid
 
 void set_error(const std::string& msg);
 

@@ -501,7 +501,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
-int gemv_grid_ctas(const Layer& L)
+int gemv_sm_count(const Layer& L)
 {
     static int sms[64] = {};
     if (!sms[L.device])
@@ -510,7 +510,12 @@ int gemv_grid_ctas(const Layer& L)
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, L.device) != cudaSuccess || v <= 0) v = 148;
         sms[L.device] = v;
     }
-    return sms[L.device] * CTAS_PER_SM;   // CTAS_PER_SM CTAs (9 warps, <= 64 KB ring each) per SM
+    return sms[L.device];
+}
+
+int gemv_grid_ctas(const Layer& L)
+{
+    return gemv_sm_count(L) * CTAS_PER_SM;   // CTAS_PER_SM CTAs (9 warps, <= 64 KB ring each) per SM
 }
 
 WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)

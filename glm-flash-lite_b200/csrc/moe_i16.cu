@@ -31,10 +31,15 @@ constexpr int RB = 8;                  // tile rows per stage = one 128-input bl
 constexpr int NW = 8;                  // consumer warps = 16-column n-tiles per item (128 columns)
 constexpr int NTHR = (NW + 1) * 32;
 #ifndef GLMX_I16_CTAS
-#define GLMX_I16_CTAS 3
+#define GLMX_I16_CTAS 2
 #endif
+#ifndef GLMX_I16_RING_KB
+#define GLMX_I16_RING_KB (GLMX_I16_CTAS >= 3 ? 64 : 96)
+#endif
+// Two CTAs of 9 warps per SM: up to 113 registers a thread (no spills in the consumer loop) and a 4-stage gate+up ring;
+// three CTAs (72 registers) measured 6 % slower on the gate+up GEMV at B = 64.
 constexpr int CTAS = GLMX_I16_CTAS;                 // CTAs per SM
-constexpr int RING = (CTAS >= 3 ? 64 : 96) * 1024;   // ring bytes per CTA
+constexpr int RING = GLMX_I16_RING_KB * 1024;       // ring bytes per CTA
 
 template <int K0, int K1, int NMAT>
 struct CfgI
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                 const uint8_t* mat = st + (m == 0 ? 0 : C::MAT0);
                 const int row_bytes = m == 0 ? C::ROW0 : C::ROW1;
                 const int tb = m == 0 ? C::TB0 : C::TB1;
-                const uint8_t* act = st + C::MAT0 + C::MAT1 + m * I16_ACT_BYTES + lane * 8;
+                const uint8_t* act = st + C::MAT0 + C::MAT1 + m * I16_ACT_BYTES + lane * 16;
                 int acc[4][4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0;
@@ -260,10 +265,12 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
                         decode_words<K1>(mat + (2 * p + 1) * row_bytes + warp * tb, L1, xb);
                     }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
+                    for (int ch = 0; ch < 2; ++ch)
                     {
-                        const uint2 bb = *reinterpret_cast<const uint2*>(act + (p * 4 + c) * 256);
-                        imma_u8s8(acc[c], xa[c], xa[c + 4], xb[c], xb[c + 4], bb.x, bb.y);
+                        // the B fragments of classes 2ch and 2ch + 1: one 16-byte load
+                        const uint4 bb = *reinterpret_cast<const uint4*>(act + (p * 2 + ch) * 512);
+                        imma_u8s8(acc[2 * ch], xa[2 * ch], xa[2 * ch + 4], xb[2 * ch], xb[2 * ch + 4], bb.x, bb.y);
+                        imma_u8s8(acc[2 * ch + 1], xa[2 * ch + 1], xa[2 * ch + 5], xb[2 * ch + 1], xb[2 * ch + 5], bb.z, bb.w);
                     }
                 }
                 if (SPLIT)      // also for S = 1: one epilogue form per variant keeps the split variant's registers low
@@ -340,7 +347,8 @@ __global__ void __launch_bounds__(NTHR, CTAS) gemv_i16_kernel(GemvI16Args a)
 }
 
 // ---- quantisation of one 128-block held by a warp (v[q] = element lane + 32 q) into the replicated B layout ----
-// Layout of one (job, projection, block): [pair p 0..3][class c 0..3][lane 0..31][b0, b1] 32-bit words; lane
+// Layout of one (job, projection, block): [pair p 0..3][class pair c / 2][lane 0..31][class c % 2][b0, b1] 32-bit words
+// (a lane's fragments of two classes are one 16-byte load); lane
 // (g, tq) holds, for token slot g/2 and plane g%2 (0 = hi, 1 = lo), the plane byte of block row 16*(2p + b) + 2tq + off_c
 // (off = 0, 1, 8, 9) replicated into the four bytes of word b.
 __device__ __forceinline__ void quantise_block(float v[4], int lane, int slot, uint8_t* actb_blk, float* sc_slot, float* psum_out)
@@ -365,8 +373,8 @@ __device__ __forceinline__ void quantise_block(float v[4], int lane, int slot, u
         const int c = (r & 1) | ((r >> 3) << 1);
         const int tqd = (r & 7) >> 1;
         const int l_hi = (2 * slot) * 4 + tqd, l_lo = (2 * slot + 1) * 4 + tqd;
-        words[((p * 4 + c) * 32 + l_hi) * 2 + b] = ((uint32_t) hi & 0xffu) * 0x01010101u;
-        words[((p * 4 + c) * 32 + l_lo) * 2 + b] = ((uint32_t) lo & 0xffu) * 0x01010101u;
+        words[(((p * 2 + (c >> 1)) * 32 + l_hi) * 2 + (c & 1)) * 2 + b] = ((uint32_t) hi & 0xffu) * 0x01010101u;
+        words[(((p * 2 + (c >> 1)) * 32 + l_lo) * 2 + (c & 1)) * 2 + b] = ((uint32_t) lo & 0xffu) * 0x01010101u;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) si += __shfl_xor_sync(0xffffffffu, si, o);
@@ -628,21 +636,27 @@ cudaError_t launch_combine(const CombineI16Args& c, int ntok, int H, cudaStream_
     }
 }
 
+}  // namespace
+
+int i16_grid_ctas(const Layer& L)
+{
+    return gemv_sm_count(L) * CTAS;
+}
+
+namespace {
+
 template <int K0, int K1, int NMAT, bool SPLIT>
 cudaError_t launch_gemv_i16_v(const Layer& L, const GemvI16Args& a, cudaStream_t st)
 {
     using C = CfgI<K0, K1, NMAT>;
     static bool attr_set[64] = {};
-    static int sms[64] = {};
     if (!attr_set[L.device])
     {
         cudaError_t e = cudaFuncSetAttribute(gemv_i16_kernel<K0, K1, NMAT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
-        if (cudaDeviceGetAttribute(&sms[L.device], cudaDevAttrMultiProcessorCount, L.device) != cudaSuccess || sms[L.device] <= 0)
-            sms[L.device] = 148;
         attr_set[L.device] = true;
     }
-    return launch_chained(gemv_i16_kernel<K0, K1, NMAT, SPLIT>, dim3(sms[L.device] * CTAS), dim3(NTHR), C::SMEM, st, a);
+    return launch_chained(gemv_i16_kernel<K0, K1, NMAT, SPLIT>, dim3(i16_grid_ctas(L)), dim3(NTHR), C::SMEM, st, a);
 }
 
 // the K-split form only where its sums buffer exists (gate/up of calls with at most I16_SPLIT_MAX_ROWS rows)
