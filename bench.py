@@ -30,10 +30,10 @@ H, I, E, TOPK = 6144, 1536, 288, 8
 EXPERT_BYTES_K3 = 3 * (H // 16) * (I // 16) * 96          # 10,616,832 trellis bytes per expert
 SCALE_BYTES = 3 * (H + I) * 2                              # suh + svh fp16 of gate, up, down: 46,080
 ROUTE_POOL = 16
-# DRAM bytes (read + write) per touched expert of one gate+up GEMV launch. I16: ncu capture of this workload itself
-# (B=64, 1829.98 MB read + 9.76 MB written over 240.4 + 1 touched experts, profiles/launches_bench_b64_i16.md). EXACT:
-# a smaller case (B=16, 57.5 experts, profiles/gemv_gateup_exact_decode_b16.md; traffic grows with the touched
-# experts). roofline.traffic = this x the touched experts of the timed launches.
+# DRAM bytes (read + write) per touched expert of one gate+up GEMV launch, from ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum). I16: a capture of this workload itself (B=64: 1829.98 MB read + 9.76 MB written over
+# 240.4 + 1 touched experts). EXACT: a smaller case (B=16: 414.9 MB + 4.0 MB over 57.5 experts; traffic grows with the
+# touched experts). roofline.traffic = this x the touched experts of the timed launches.
 GU_TRAFFIC_PER_EXPERT = {2: (1829.98e6 + 9.76e6) / 241.4, 1: (414.9e6 + 4.0e6) / 57.5}
 GU_TRAFFIC_SOURCE = {2: "bytes per launch (ncu, B=64 capture of this workload, per touched expert)",
                      1: "bytes per launch (ncu, scaled from B=16)"}
