@@ -95,7 +95,8 @@ GLMX_API int glmx_route(const glmx_layer* layer, const void* sel, int sel_dtype,
 
 /* Locate one routing array inside a workspace filled by glmx_route (for tests and callers that reuse the split):
  * which = 0 offsets int32 [E+1], 1 row_token int32 [R], 2 row_weight fp32 [R], 3 pick_row int32 [ntok*topk],
- * 4 jobs int32x4 [J] (expert, row0, m, 0), 5 plan int32 [8] (P, R, J, S_gu, S_d, ntok, topk, 0), 6 row_pick int32 [R]. */
+ * 4 jobs int32x4 [J] (expert, row0, m, 0), 5 plan int32 [8] (P, R, J, S_gu, S_d, ntok, topk, 0; two internal item
+ * counters of the I16 GEMVs follow), 6 row_pick int32 [R]. */
 GLMX_API int glmx_workspace_array(const glmx_layer* layer, int ntok, int topk, int which, size_t* offset_bytes);
 
 /* Whole routed-MoE layer on the GPU: split -> gate/up dequant-GEMV + SiLU*up -> down dequant-GEMV -> weighted
