@@ -271,22 +271,6 @@ __device__ __forceinline__ void decode_frag_tc(const uint8_t* tile, const LaneDe
     a[3] = codebook_pair(d2[2], d2[3]);
 }
 
-// decode_frag_tc from preloaded stream words (see decode_words_from)
-template <int K>
-__device__ __forceinline__ void decode_frag_tc_from(uint32_t hi, uint32_t lo, const LaneDecode<K>& L, const OnesFrag& ones,
-                                                    uint32_t a[4])
-{
-    uint32_t x[8];
-    decode_words_from<K>(hi, lo, L, x);
-    uint32_t d1[4], d2[4];
-    imma_bytesum(d1, x[0], x[4], x[1], x[5], ones.b0, ones.b1, 0x6400u);
-    imma_bytesum(d2, x[2], x[6], x[3], x[7], ones.b0, ones.b1, 0x6400u);
-    a[0] = codebook_pair(d1[0], d1[1]);
-    a[1] = codebook_pair(d1[2], d1[3]);
-    a[2] = codebook_pair(d2[0], d2[1]);
-    a[3] = codebook_pair(d2[2], d2[3]);
-}
-
 // Decoded fp16 weights of one tile as an m16n8k16 A fragment of the transposed tile (rows = output columns n, columns =
 // inputs k) in NATURAL input order: the trellis stream order is that fragment layout (ft_core.h:48-61 PERM: lane
 // (g, tq)'s stream weights 8*lane .. 8*lane+7 sit at (k, n) = (2tq, g), (2tq+1, g), (2tq+8, g), (2tq+9, g), then the
