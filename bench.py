@@ -136,10 +136,6 @@ def cpu_reference_run(B: int, seconds: float, threads: int, seed: int = 0):
 
 
 def cpu_threads():
-    try:
-        from oracle.oracle import REF_SO  # noqa: F401
-    except Exception:
-        pass
     n = len(os.sched_getaffinity(0))
     return max(1, n - 2) if n > 3 else n
 
