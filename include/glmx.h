@@ -73,15 +73,23 @@ typedef struct
                                          (kernels/cpu_avx2/ft_tier_cu.cu:22, glm53/cpu_tier.py:293-299) */
 } glmx_layer_desc;
 
+/* No counterpart: the ABI version (GLMX_ABI_VERSION-checked by the Python loader) and the calling thread's last error
+ * message. The reference raises its argument errors as TORCH_CHECK RuntimeErrors (kernels/cpu_avx2/ft_tier_ext.cpp:143,
+ * 166); here every entry returns a GLMX_E_* status and leaves the message for glmx_last_error. */
 GLMX_API int glmx_version(void);
 GLMX_API const char* glmx_last_error(void);
 
+/* tier_add_layer (kernels/cpu_avx2/ft_tier_ext.cpp:160-183): registers one layer's expert pointer table and scales.
+ * The trellis tensors stay the caller's (borrowed, as the reference keeps them alive with T->keep, 154, 184). */
 GLMX_API int glmx_layer_create(const glmx_layer_desc* desc, glmx_layer** out);
+/* The per-layer part of tier_stop (kernels/cpu_avx2/ft_tier_ext.cpp:837): frees the layer's device table and tensor maps. */
 GLMX_API int glmx_layer_destroy(glmx_layer* layer);
 /* tier_set_act_limit (kernels/cpu_avx2/ft_tier_ext.cpp:635) */
 GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
 
-/* Bytes of caller-provided device workspace a forward over `ntok` tokens with `topk` picks each needs. */
+/* Bytes of caller-provided device workspace a forward over `ntok` tokens with `topk` picks each needs. No counterpart:
+ * tier_forward allocates its output per call (torch::zeros, kernels/cpu_avx2/ft_tier_ext.cpp:895); here the caller owns
+ * all device memory, allocated once and reused, so a forward allocates nothing. */
 GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk);
 
 /* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
@@ -93,7 +101,9 @@ GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk
 GLMX_API int glmx_route(const glmx_layer* layer, const void* sel, int sel_dtype, const void* w, int w_dtype, int ntok, int topk,
                void* workspace, size_t workspace_bytes, void* stream);
 
-/* Locate one routing array inside a workspace filled by glmx_route (for tests and callers that reuse the split):
+/* No counterpart (the split's outputs in the reference are ft_split's sel_out / w_out / hpicks,
+ * kernels/cpu_avx2/ft_tier_cu.cu:238-271). Locate one routing array inside a workspace filled by glmx_route (for tests
+ * and callers that reuse the split):
  * which = 0 offsets int32 [E+1], 1 row_token int32 [R], 2 row_weight fp32 [R], 3 pick_row int32 [ntok*topk],
  * 4 jobs int32x4 [J] (expert, row0, m, 0), 5 plan int32 [8] (P, R, J, S_gu, S_d, ntok, topk, 0; two internal item
  * counters of the I16 GEMVs follow), 6 row_pick int32 [R]. */
@@ -108,7 +118,8 @@ GLMX_API int glmx_moe_forward(const glmx_layer* layer, const void* x, int x_dtyp
                      const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
                      void* workspace, size_t workspace_bytes, void* stream);
 
-/* glmx_moe_forward that also records `events` (GLMX_PHASES cudaEvent_t, or NULL entries to skip) on `stream` before the
+/* The per-phase timers of tier_stats (kernels/cpu_avx2/ft_tier_ext.cpp:906-914) as CUDA events:
+ * glmx_moe_forward that also records `events` (GLMX_PHASES cudaEvent_t, or NULL entries to skip) on `stream` before the
  * split, after the split, after the input transform, after gate/up, after down and after the combine, so a caller
  * can time each kernel on the launching stream. */
 #define GLMX_PHASES 6
@@ -143,7 +154,8 @@ GLMX_API int glmx_check(const glmx_layer* layer, int ntok, int topk, void* works
  * *flag (the bit glmx_check reports for a stalled forward). The kernel returns normally; the context stays usable. */
 GLMX_API int glmx_selftest_bounded_wait(int timeout_us, int* flag, void* stream);
 
-/* Expert-parallel return over peer memory. A rank of `world` holds a shard of the experts (first_expert, n_experts)
+/* No counterpart (the reference runs every expert of a layer on one GPU and its CPU tier; expert sharding over GPUs is
+ * this library's). Expert-parallel return over peer memory. A rank of `world` holds a shard of the experts (first_expert, n_experts)
  * and runs the layer over all ranks' gathered rows, rows_per_rank consecutive rows per rank (ntok = world *
  * rows_per_rank). glmx_moe_forward_peer computes like glmx_moe_forward but, instead of writing `out`, its combine stores
  * token t's fp32 row into rank (t / rows_per_rank)'s receive buffer at [seq & 1][rank][t % rows_per_rank], through the
@@ -163,13 +175,13 @@ GLMX_API int glmx_moe_forward_peer(const glmx_layer* layer, const void* x, int x
                                    void* workspace, size_t workspace_bytes, void* stream);
 GLMX_API int glmx_peer_reduce(const float* recv, const int* flags, int world, int rows_per_rank, int hidden, int seq,
                               void* out, int out_dtype, int* err, void* stream);
-/* The shard's picks of the gathered rows, one kernel: route int32 [rows][2 * topk] = global expert ids then the fp32
+/* No counterpart (expert parallelism). The shard's picks of the gathered rows, one kernel: route int32 [rows][2 * topk] = global expert ids then the fp32
  * weights' bits; loc int32 / w fp32 [rows][topk + (shared ? 1 : 0)]: ids in [first, first + n) become 0 .. n - 1 with
  * their weight, others -1 with weight 0; with shared, a last column of local id n (weight 1) on rows
  * [own_begin, own_end) (the rank's own rows) and -1 elsewhere. */
 GLMX_API int glmx_ep_split(const int* route, int rows, int topk, int first, int n, int shared, int own_begin, int own_end,
                            int* loc, float* w, void* stream);
-/* CUDA IPC for those buffers: glmx_ipc_alloc makes a zeroed device allocation of its own (the mapping in another
+/* No counterpart (expert parallelism). CUDA IPC for those buffers: glmx_ipc_alloc makes a zeroed device allocation of its own (the mapping in another
  * process then starts at the buffer), glmx_ipc_handle its handle (GLMX_IPC_HANDLE_BYTES bytes), glmx_ipc_open maps a
  * peer's handle, glmx_ipc_close / glmx_ipc_free undo them. */
 #define GLMX_IPC_HANDLE_BYTES 64
