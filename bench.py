@@ -67,6 +67,8 @@ class ClockSampler:
                 self.first.set()
 
     def __enter__(self):
+        if self.index < 0:                 # sampling off (the caller samples around a larger region itself)
+            return self
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -361,25 +363,19 @@ def run_router(args, dev):
     print(json.dumps(line), flush=True)
 
 
-def run_prefill(args, dev):
-    """configs[2]: one layer (288 routed + 1 shared) at prefill, T tokens (4096) of bf16 activations ~ N(0,1), expert
-    popularity Zipf(1.1) over a seeded permutation, top-8. EXACT mode through the tensor-core GEMM path. Metric:
-    TFLOP/s of useful work = 2 * 3 * H * I * T * (8 + 1) per call / device time."""
+def prefill_layer(dev, seed=4321):
+    """configs[2]'s layer: 288 routed + 1 shared expert of configs[0]'s shape, K=3 (the decode layer's construction)."""
     import torch
-    from glmx import MoELayer, _lib, synth
-
-    T = args.tokens
     g = torch.Generator(device=dev)
-    g.manual_seed(4321)
-    et = E + 1
-    bank = torch.randint(0, 256, (et * EXPERT_BYTES_K3,), dtype=torch.uint8, device=dev, generator=g)
-    proj = (H // 16) * (I // 16) * 96
-    ptrs = torch.tensor([[bank.data_ptr() + e * EXPERT_BYTES_K3 + p * proj for p in range(3)] for e in range(et)],
-                        dtype=torch.int64)
-    sign = lambda shape: torch.where(torch.rand(shape, device=dev, generator=g) < 0.5, -1.0, 1.0)
-    suh = [sign((et, k)).half() for k in (H, H, I)]
-    svh = [(sign((et, n)) * (0.02 + 0.005 * torch.randn((et, n), device=dev, generator=g)).abs()).half() for n in (I, I, H)]
-    layer = MoELayer(H, I, E, ptrs, suh, svh, bits=(3, 3, 3), has_shared=True, keep=[bank], device=dev)
+    g.manual_seed(seed)
+    return decode_layer(dev, g, E), g
+
+
+def prefill_measure(layer, dev, g, T, steps, warmup, e2e=True, clocks=True):
+    """configs[2] on `layer`: T tokens of bf16 activations ~ N(0,1), expert popularity Zipf(1.1) over a seeded
+    permutation, top-8, EXACT mode through the tensor-core GEMM path. Returns the measurements as a dict."""
+    import torch
+    from glmx import _lib, synth
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
     npool = 4
@@ -390,56 +386,74 @@ def run_prefill(args, dev):
     out = torch.empty((T, H), dtype=torch.float32, device=dev)
     mode = _lib.MODE_EXACT | _lib.PATH_GEMM
     flop = 2.0 * 3 * H * I * T * (TOPK + 1)
-    steps = args.steps
     ph = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.PHASES)] for _ in range(steps)]
-    for i in range(args.warmup):
+    for i in range(warmup):
         layer.forward(x, sel[i % npool], wts[i % npool], out=out, mode=mode)
     torch.cuda.synchronize(dev)
     t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
     clk_idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]) if os.environ.get("CUDA_VISIBLE_DEVICES") else 0
-    with ClockSampler(clk_idx) as cs:
+    with ClockSampler(clk_idx if clocks else -1) as cs:
         t0.record(stream)
         for i in range(steps):
             layer.forward(x, sel[i % npool], wts[i % npool], out=out, mode=mode, events=ph[i])
         t1.record(stream)
         torch.cuda.synchronize(dev)
-    clocks = cs.summary()
     flags = layer.check_device(T, TOPK)
     if flags:
         raise RuntimeError(f"device error flags {flags}")
     T_ms = t0.elapsed_time(t1)
     step_ms = [ph[i][0].elapsed_time(ph[i][5]) for i in range(steps)]
     phase_ms = [[ph[i][k].elapsed_time(ph[i][k + 1]) for k in range(_lib.PHASES - 1)] for i in range(steps)]
-    tflops = flop * steps / (T_ms / 1e3) / 1e12
     gu_ms = sum(p[2] for p in phase_ms)
     d_ms = sum(p[3] for p in phase_ms)
-    gu_tflops = (2.0 * 2 * H * I * T * (TOPK + 1)) * steps / (gu_ms / 1e3) / 1e12
-    d_tflops = (2.0 * H * I * T * (TOPK + 1)) * steps / (d_ms / 1e3) / 1e12
-    phase_share = [sum(p[k] for p in phase_ms) / sum(step_ms) for k in range(_lib.PHASES - 1)]
-    # rows per expert of the routings (tile efficiency of the 128-row jobs)
     counts = [np.bincount(s.reshape(-1), minlength=E) for s, _ in routes]
-    rows_real = np.mean([c.sum() + T for c in counts])
-    rows_tiles = np.mean([(np.ceil(c / 128).sum() + np.ceil(T / 128)) * 128 for c in counts])
+    res = dict(T_ms=T_ms, steps=steps, flop=flop, peak=pk, peak_kind=pk_kind, x=x,
+               tflops=flop * steps / (T_ms / 1e3) / 1e12,
+               gu_tflops=(2.0 * 2 * H * I * T * (TOPK + 1)) * steps / (gu_ms / 1e3) / 1e12,
+               d_tflops=(2.0 * H * I * T * (TOPK + 1)) * steps / (d_ms / 1e3) / 1e12,
+               phase_share=[sum(p[k] for p in phase_ms) / sum(step_ms) for k in range(_lib.PHASES - 1)],
+               rows=np.mean([c.sum() + T for c in counts]),
+               tile_rows=np.mean([(np.ceil(c / 128).sum() + np.ceil(T / 128)) * 128 for c in counts]),
+               clocks=cs.summary() if clocks else None)
+    if e2e:
+        # bf16 activations and routing from pinned host memory, fp32 result back
+        x_h = x.cpu().pin_memory(); s_h = [s.cpu().pin_memory() for s in sel]; w_h = [w.cpu().pin_memory() for w in wts]
+        out_h = torch.empty((T, H), dtype=torch.float32).pin_memory()
+        x_d = torch.empty_like(x); s_d = torch.empty_like(sel[0]); w_d = torch.empty_like(wts[0])
 
-    # e2e: bf16 activations and routing from pinned host memory, fp32 result back
-    x_h = x.cpu().pin_memory(); s_h = [s.cpu().pin_memory() for s in sel]; w_h = [w.cpu().pin_memory() for w in wts]
-    out_h = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    x_d = torch.empty_like(x); s_d = torch.empty_like(sel[0]); w_d = torch.empty_like(wts[0])
-    def e2e_step(i):
-        x_d.copy_(x_h, non_blocking=True); s_d.copy_(s_h[i % npool], non_blocking=True); w_d.copy_(w_h[i % npool], non_blocking=True)
-        layer.forward(x_d, s_d, w_d, out=out, mode=mode)
-        out_h.copy_(out, non_blocking=True)
-    for i in range(args.warmup):
-        e2e_step(i)
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(steps):
-        e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
+        def e2e_step(i):
+            x_d.copy_(x_h, non_blocking=True); s_d.copy_(s_h[i % npool], non_blocking=True)
+            w_d.copy_(w_h[i % npool], non_blocking=True)
+            layer.forward(x_d, s_d, w_d, out=out, mode=mode)
+            out_h.copy_(out, non_blocking=True)
+        for i in range(warmup):
+            e2e_step(i)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            e2e_step(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        res["e2e_tflops"] = flop * steps / (e0.elapsed_time(e1) / 1e3) / 1e12
+        res["h2d"] = T * H * 2 + T * TOPK * 8
+        res["d2h"] = T * H * 4
+    return res
 
+
+def run_prefill(args, dev):
+    """configs[2]: one layer (288 routed + 1 shared) at prefill, T tokens (4096) of bf16 activations ~ N(0,1), expert
+    popularity Zipf(1.1) over a seeded permutation, top-8. EXACT mode through the tensor-core GEMM path. Metric:
+    TFLOP/s of useful work = 2 * 3 * H * I * T * (8 + 1) per call / device time."""
+    from glmx import synth
+    T = args.tokens
+    layer, g = prefill_layer(dev)
+    r = prefill_measure(layer, dev, g, T, args.steps, args.warmup)
+    x = r["x"]
+    flop, pk, pk_kind, clocks = r["flop"], r["peak"], r["peak_kind"], r["clocks"]
+    steps = args.steps
+    T_ms, tflops, gu_tflops, d_tflops = r["T_ms"], r["tflops"], r["gu_tflops"], r["d_tflops"]
+    phase_share, rows_real, rows_tiles = r["phase_share"], r["rows"], r["tile_rows"]
     cpu = None
     if not args.no_cpu_baseline:
         try:
@@ -484,8 +498,7 @@ def run_prefill(args, dev):
                      "down_achieved": d_tflops, "layer_achieved": tflops, "layer_frac": tflops / peak},
         "phase_share": dict(zip(["route", "prep", "gemm_gateup+epilogue", "gemm_down", "combine"], phase_share)),
         "cpu_baseline": cpu,
-        "e2e": {"value": flop * steps / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": T * H * 2 + T * TOPK * 8, "d2h_bytes_per_step": T * H * 4},
+        "e2e": {"value": r["e2e_tflops"], "unit": "TFLOP/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
         "gpu_launches": 6 * steps,
         "clocks": clocks,
     }
@@ -636,8 +649,11 @@ def main():
                     help="decode: configs[1] (the headline); prefill: configs[2] (4096 tokens, Zipf routing, TFLOP/s); "
                          "sweep: configs[4] (bitrates x skews x batch sizes)")
     ap.add_argument("--tokens", type=int, default=4096, help="prefill tokens")
-    ap.add_argument("--mode", type=int, default=2, choices=[1, 2], help="1 EXACT (fp16 weights, fp32 tensor-core sums), "
-                    "2 I16 (int16 activations, exact integer tensor-core sums; bit-identical to the reference's I16 mode)")
+    ap.add_argument("--mode", type=int, default=1, choices=[1, 2], help="1 EXACT (fp16 codebook weights, fp32 "
+                    "accumulation: the reference's EXACT arithmetic, the headline), 2 I16 (int16 activations, exact "
+                    "integer tensor-core sums; bit-identical to the reference's I16 kernel, outside the 2e-3 bar at H=6144)")
+    ap.add_argument("--no-extras", action="store_true", help="default line without the other mode's decode number and the "
+                    "configs[2] prefill keys")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -679,7 +695,8 @@ def main():
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
 
-    def device_run(B, steps, warmup, flush_l2=False):
+    def device_run(B, steps, warmup, flush_l2=False, mode=None):
+        mode = args.mode if mode is None else mode
         routes = make_routes(B, 1000 + 97 * rank)
         sel = [torch.from_numpy(s).to(dev) for s, _ in routes]
         wts = [torch.from_numpy(w).to(dev) for _, w in routes]
@@ -689,7 +706,7 @@ def main():
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush_l2 else None
         ph = [[torch.cuda.Event(enable_timing=True) for _ in range(_lib.PHASES)] for _ in range(steps)]
         for i in range(warmup):
-            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, mode=args.mode)
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, mode=mode)
         if dist:
             dist.barrier()
         torch.cuda.synchronize(dev)
@@ -699,7 +716,7 @@ def main():
         for i in range(steps):
             if flush is not None:
                 flush.zero_()
-            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, events=ph[i], mode=args.mode)
+            layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], out=out, events=ph[i], mode=mode)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if dist:
@@ -791,6 +808,32 @@ def main():
                          "hbm_gbs": sum(lb) / (sum(rs["step_ms"]) / 1e3) / 1e9,
                          "unique_experts": statistics.mean(rs["uniq"]), "l2_flushed": rs["flushed"]}
 
+    # ---- the other decode mode and configs[2] prefill on the same layer (extra keys of the line) ----
+    extras = {}
+    if not args.no_extras and world == 1:
+        om = 2 if args.mode == 1 else 1
+        ro = device_run(B, max(20, args.steps // 3), 3, flush_l2=B < 32, mode=om)
+        lbo, gbo = step_bytes(ro["uniq"], len(ro["step_ms"]))
+        extras["other_mode"] = {
+            "mode": {1: "EXACT", 2: "I16"}[om],
+            "tok_per_s": B * len(ro["step_ms"]) / (ro["total_ms"] / 1e3), "ms_per_step": ro["total_ms"] / len(ro["step_ms"]),
+            "gateup_gbs": sum(gbo) / (sum(p[2] for p in ro["phase_ms"]) / 1e3) / 1e9,
+            "layer_gbs": sum(lbo) / (sum(ro["step_ms"]) / 1e3) / 1e9,
+            "note": "I16: int16 activations per 128-block, bit-identical to the reference's I16 kernel; 4-6e-3 x RMS from "
+                    "the fp64 EXACT restatement at H=6144, outside the north-star bar" if om == 2 else
+                    "EXACT: the reference's EXACT arithmetic"}
+        pr = prefill_measure(layer, dev, g, args.tokens, steps=6, warmup=3, e2e=True, clocks=False)
+        pk_tc = pk["bf16_tflops"]
+        extras["prefill"] = {
+            "workload": f"configs[2]: {args.tokens} tokens, Zipf(1.1) over 288 routed experts + shared, top-8, bf16 "
+                        "activations, EXACT on the tensor-core GEMM path (the same layer)",
+            "tflops": pr["tflops"], "ms_per_call": pr["T_ms"] / pr["steps"], "gateup_tflops": pr["gu_tflops"],
+            "down_tflops": pr["d_tflops"], "gateup_frac": pr["gu_tflops"] / pk_tc, "layer_frac": pr["tflops"] / pk_tc,
+            "peak_tflops": pk_tc, "peak_kind": pk_kind + " bf16 burst",
+            "e2e_tflops": pr.get("e2e_tflops"), "h2d_bytes_per_step": pr.get("h2d"), "d2h_bytes_per_step": pr.get("d2h"),
+            "tile_efficiency": pr["rows"] / pr["tile_rows"]}
+        del pr
+
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -834,6 +877,7 @@ def main():
         "gpu_launches": (6 if args.mode == 2 else 5) * args.steps,
         "clocks": clocks,
         "sweep": sweep,
+        **extras,
     }
     print(json.dumps(line), flush=True)
 

@@ -111,6 +111,8 @@ int glmx_layer_destroy(glmx_layer* l)
     return GLMX_OK;
 }
 
+int glmx_layer_device(const glmx_layer* l) { return l ? l->L.device : GLMX_E_ARG; }
+
 int glmx_layer_set_act_limit(glmx_layer* l, float limit)
 {
     if (!l) return fail(GLMX_E_ARG, "glmx_layer_set_act_limit: null layer");
@@ -218,7 +220,7 @@ static int forward_impl(const glmx_layer* l, const void* x, int x_dtype, int nto
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     cudaError_t e = cudaSuccess;
     if (events && events[0]) e = cudaEventRecord(static_cast<cudaEvent_t>(events[0]), st);
-    const int maxm = base == GLMX_MODE_I16 ? I16_MAXM : gemm ? PF_MAXM : MAXM;
+    const int maxm = base == GLMX_MODE_I16 ? I16_MAXM : gemm ? PF_MAXM : EXACT_MAXM;
     // the K-split plan is made for the grid of the GEMV that follows
     const int plan_grid = base == GLMX_MODE_I16 ? i16_grid_ctas(l->L) : grid;
     if (e == cudaSuccess) e = launch_route(l->L, sel, sel_dtype == GLMX_I64, w, w_dtype, ntok, topk, maxm, wsb, lay, plan_grid, st);

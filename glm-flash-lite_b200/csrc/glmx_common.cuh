@@ -204,6 +204,16 @@ __host__ __device__ constexpr int perm16(int h) { return (h & 8) | ((h & 4) ? ((
 // position h of input row r within its 16-row tile (inverse of perm16)
 __host__ __device__ constexpr int perm16_inv(int r) { return (r & 8) | ((r & 1) ? (4 | ((r & 7) >> 1)) : ((r & 7) >> 1)); }
 
+// Position (in fp16 elements) of input k (0..127) of a 128-input block in the EXACT GEMV's activation layout: for each
+// pair of 16-row tile rows (r = 2 rp, 2 rp + 1) and each lane quad tq, the 8 values that lane (g, tq) multiplies with its
+// decode_frag_tc weights: rows PERM16(2tq), PERM16(2tq+1), PERM16(2tq)+8, PERM16(2tq+1)+8 of tile row 2 rp, then of
+// tile row 2 rp + 1. A lane reads them with one 16-byte load; the four quads read one contiguous 64-byte run.
+__host__ __device__ constexpr int gemv_xpos(int k)
+{
+    return (k >> 5) * 32 + (((perm16_inv(k & 15) & 7) >> 1) * 8) + (((k >> 4) & 1) * 4) + ((perm16_inv(k & 15) & 1) |
+           ((perm16_inv(k & 15) >> 3) << 1));
+}
+
 __device__ __forceinline__ void imma_bytesum(uint32_t d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                              uint32_t b1, uint32_t c)
 {
@@ -288,13 +298,6 @@ __device__ __forceinline__ void decode_frag_nat(uint32_t hi, uint32_t lo, const 
     a[1] = codebook_pair(s[4], s[5]);     // n = g + 8, k = 2tq, 2tq+1
     a[2] = codebook_pair(s[2], s[3]);     // n = g,     k = 2tq+8, 2tq+9
     a[3] = codebook_pair(s[6], s[7]);     // n = g + 8, k = 2tq+8, 2tq+9
-}
-
-__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
-{
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // ---- hyper-connection update of one column (exllamav3 hc_apply; glm53/k_hcfuse.py:62-91) --------------------------

@@ -124,6 +124,10 @@ cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int 
                                uint8_t* ws, const WsLayout& lay, cudaStream_t st, const HcOut* hc = nullptr);
 
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
+#ifndef GLMX_EXACT_MAXM
+#define GLMX_EXACT_MAXM 4
+#endif
+constexpr int EXACT_MAXM = GLMX_EXACT_MAXM;   // rows per job of the EXACT decode GEMV (per-row accumulators in registers)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
 // one (job, 128-input block) record of the I16 activations, laid out as a GEMV stage holds it: the nmat projections'
 // planes, then their 4 scales (16 bytes each)

@@ -29,25 +29,28 @@ namespace {
 constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one 128-input block
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
-constexpr int XROW = 272;    // bytes per staged activation row: 128 fp16 + 16 bytes pad (conflict-free B loads)
+constexpr int XROW = 256;    // bytes per staged activation row: one 128-input block, fp16, in the lane order of gemv_xpos
 #ifndef GLMX_EXACT_CTAS
 #define GLMX_EXACT_CTAS 3
 #endif
 constexpr int CTAS_PER_SM = GLMX_EXACT_CTAS;
-constexpr int RING_BYTES = (CTAS_PER_SM >= 3 ? 64 : 96) * 1024;    // per CTA; CTAS_PER_SM rings share an SM
+constexpr int RING_BYTES = (CTAS_PER_SM >= 3 ? 56 : 88) * 1024;    // per CTA; CTAS_PER_SM rings share an SM
 
+// One pipeline stage holds RB k-tile rows x 8 tiles of ONE matrix (an item of the gate/up kernel runs all stages of
+// gate, then all stages of up) and the job's activation rows for that block.
 template <int K0, int K1, int NMAT>
 struct Cfg
 {
     static constexpr int TB0 = 32 * K0, TB1 = 32 * K1;
     static constexpr int ROW0 = 8 * TB0, ROW1 = 8 * TB1;
-    static constexpr int MAT0 = RB * ROW0, MAT1 = NMAT > 1 ? RB * ROW1 : 0;
-    static constexpr int XS = MAXM * XROW;
-    static constexpr int STAGE = (MAT0 + MAT1 + NMAT * XS + 127) / 128 * 128;   // tensor copies land 128-byte aligned
+    static constexpr int MAT = RB * (ROW0 > ROW1 ? ROW0 : ROW1);
+    static constexpr int XS = EXACT_MAXM * XROW;
+    static constexpr int STAGE = (MAT + XS + 127) / 128 * 128;   // tensor copies land 128-byte aligned
     static constexpr int NST = RING_BYTES / STAGE < 3 ? 3 : (RING_BYTES / STAGE > 12 ? 12 : RING_BYTES / STAGE);
-    static constexpr int RED = NMAT * MAXM * 128 * 4;
+    static constexpr int RED = NMAT * EXACT_MAXM * 128 * 8;      // (hi, lo) pairs
     static constexpr int SMEM = NST * STAGE + RED + 2 * NST * 8;
-    static_assert(STAGE % 128 == 0 && MAT0 % 128 == 0 && (MAT0 + MAT1) % 16 == 0, "stage alignment");
+    static_assert(STAGE % 128 == 0 && MAT % 128 == 0, "stage alignment");
+    static_assert(EXACT_MAXM == 4 || EXACT_MAXM == 8, "EXACT GEMV jobs of 4 or 8 rows");
 };
 
 struct GemvArgs
@@ -59,12 +62,12 @@ struct GemvArgs
     int proj0;                   // projection index of matrix 0 (0 = gate, 2 = down)
     int kt, ntn;                 // k-tiles and n-tiles of the matrix
     int kdim, ndim;              // K and N
-    const __half* xin0; const __half* xin1;       // staged activation rows [R][kdim]
+    const __half* xin0; const __half* xin1;       // staged activation rows [R][kdim] (gemv_xpos order per block)
     const __half* svh0; const __half* svh1;       // [E_total][ndim]
     const __half* suh_next;                       // gate/up: suh of down [E_total][ndim]
     __half* xd;                                   // gate/up epilogue output [R][ndim]
     float* y;                                     // down epilogue output [R][ndim]
-    float* partials; int* counters; int* err;
+    float2* partials; int* counters; int* err;
     float act_limit;
 };
 
@@ -72,13 +75,133 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
 
+// 8-term partial dot product of a lane's two tile rows (2rp, 2rp+1) with one token, in fp32 with exact fp16 x fp16
+// products: a chain of mixed-precision FMAs (fp16 operands, fp32 accumulate, one rounding each) starting from zero,
+// row 2rp's four terms (weights w01 = (w0, w1), w23 = (w2, w3) against x.x, x.y) then row 2rp+1's (v01, v23 against
+// x.z, x.w).
+__device__ __forceinline__ float dot8(uint32_t w01, uint32_t w23, uint32_t v01, uint32_t v23, uint4 xv)
+{
+    float d;
+    asm("{\n .reg .f16 a0, a1, a2, a3, b0, b1, b2, b3, x0, x1, x2, x3, x4, x5, x6, x7;\n"
+        " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {b0, b1}, %3;\n mov.b32 {b2, b3}, %4;\n"
+        " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
+        " fma.rn.f32.f16 %0, a0, x0, 0f00000000;\n fma.rn.f32.f16 %0, a1, x1, %0;\n"
+        " fma.rn.f32.f16 %0, a2, x2, %0;\n fma.rn.f32.f16 %0, a3, x3, %0;\n"
+        " fma.rn.f32.f16 %0, b0, x4, %0;\n fma.rn.f32.f16 %0, b1, x5, %0;\n"
+        " fma.rn.f32.f16 %0, b2, x6, %0;\n fma.rn.f32.f16 %0, b3, x7, %0;\n}"
+        : "=f"(d)
+        : "r"(w01), "r"(w23), "r"(v01), "r"(v23), "r"(xv.x), "r"(xv.y), "r"(xv.z), "r"(xv.w));
+    return d;
+}
+
+// One pipeline stage of one matrix for an M-row job. Lane (g, tq) of consumer warp w decodes its 8 weights of tiles
+// (2rp, w) and (2rp + 1, w) (decode_frag_tc: output columns g and g + 8, input rows PERM16(2tq), PERM16(2tq+1) and the
+// same + 8), forms for each row of the job the 8-term partial of each of its two columns and adds it into that
+// column's block sum. The lane's activations of the two tile rows are one 16-byte load (gemv_xpos); the four quads'
+// loads fill one 64-byte run.
+template <int K, int M>
+__device__ __forceinline__ void stage_fma(const uint8_t* st, int row_bytes, int t_off, int x_off, const LaneDecode<K>& L,
+                                          const OnesFrag& ones, float blk[M][2])
+{
+#pragma unroll
+    for (int rp = 0; rp < RB / 2; ++rp)
+    {
+        uint32_t a[4], b[4];
+        decode_frag_tc<K>(st + t_off + (2 * rp) * row_bytes, L, ones, a);
+        decode_frag_tc<K>(st + t_off + (2 * rp + 1) * row_bytes, L, ones, b);
+        const uint8_t* xr = st + x_off + rp * 64;
+#pragma unroll
+        for (int i = 0; i < M; ++i)
+        {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xr + i * XROW);
+            blk[i][0] = __fadd_rn(blk[i][0], dot8(a[0], a[2], b[0], b[2], xv));
+            blk[i][1] = __fadd_rn(blk[i][1], dot8(a[1], a[3], b[1], b[3], xv));
+        }
+    }
+}
+
+// Sum of the four lanes (tq = 0..3) of a quad of (hi, lo) pairs: TwoSum of the hi parts (exact error term), lo parts
+// added; every lane of the quad ends with the same pair.
+__device__ __forceinline__ void quad_sum(float& h, float& l)
+{
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1)
+    {
+        const float h2 = __shfl_xor_sync(0xffffffffu, h, off), l2 = __shfl_xor_sync(0xffffffffu, l, off);
+        const float s = __fadd_rn(h, h2);
+        const float bb = __fsub_rn(s, h);
+        const float e = __fadd_rn(__fsub_rn(h, __fsub_rn(s, bb)), __fsub_rn(h2, bb));
+        l = __fadd_rn(__fadd_rn(l, l2), e);
+        h = s;
+    }
+}
+
+// The k-stages of one item for an M-row job: matrix by matrix, each lane keeps per (row, column) a block sum (fp32)
+// and a running (hi, lo) pair fed once per 128-input block by Fast2Sum, so the rounding error stays at the level of
+// one 128-input block; at the end the quad's pairs are summed (quad_sum) and the pair goes to red[mat][row][col].
+template <int K0, int K1, int NMAT, int M>
+__device__ __forceinline__ void item_consume(uint8_t* ring, uint64_t* full, uint64_t* empty, float2* red, int kqs,
+                                             int& s, uint32_t& ph, volatile int* s_abort, int* err, int warp, int lane,
+                                             const LaneDecode<K0>& L0, const LaneDecode<K1>& L1, const OnesFrag& ones)
+{
+    using C = Cfg<K0, K1, NMAT>;
+    const int g = lane >> 2, tq = lane & 3;
+    const int x_off = C::MAT + tq * 16;
+#pragma unroll 1
+    for (int m = 0; m < NMAT; ++m)
+    {
+        float hi[M][2], lo[M][2];
+#pragma unroll
+        for (int i = 0; i < M; ++i) hi[i][0] = hi[i][1] = lo[i][0] = lo[i][1] = 0.0f;
+#pragma unroll 1
+        for (int q = 0; q < kqs; ++q)
+        {
+            if (!*s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(err, ERR_TIMEOUT_FULL); *s_abort = 1; }
+            const uint8_t* st = ring + s * C::STAGE;
+            float blk[M][2];
+#pragma unroll
+            for (int i = 0; i < M; ++i) blk[i][0] = blk[i][1] = 0.0f;
+            if (NMAT == 1 || m == 0) stage_fma<K0, M>(st, C::ROW0, warp * C::TB0, x_off, L0, ones, blk);
+            else stage_fma<K1, M>(st, C::ROW1, warp * C::TB1, x_off, L1, ones, blk);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == C::NST) { s = 0; ph ^= 1u; }
+#pragma unroll
+            for (int i = 0; i < M; ++i)
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                {
+                    const float sum = __fadd_rn(hi[i][c], blk[i][c]);
+                    lo[i][c] = __fadd_rn(lo[i][c], __fsub_rn(blk[i][c], __fsub_rn(sum, hi[i][c])));
+                    hi[i][c] = sum;
+                }
+        }
+        float2* rm = red + m * EXACT_MAXM * 128;
+        const int o = warp * 16 + g;
+#pragma unroll
+        for (int i = 0; i < M; ++i)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+            {
+                float h = hi[i][c], l = lo[i][c];
+                quad_sum(h, l);
+                if (tq == 0) rm[i * 128 + o + 8 * c] = make_float2(h, l);
+            }
+    }
+}
+
+// EXACT-mode GEMV (one persistent kernel per phase). Items (job, 128-column block, K split); per item the producer
+// warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per row), the 8
+// consumer warps decode and multiply-accumulate on the CUDA cores (dot8, stage_fma) - the tensor pipe only forms the
+// trellis byte sums, whose integer results are exact. The hardware MMA's fp32 accumulation is not used for the dot
+// products: it truncates the aligned sum of each MMA to about the precision of its largest addend.
 template <int K0, int K1, int NMAT, bool GATEUP>
-__global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
+__global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 {
     using C = Cfg<K0, K1, NMAT>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;
-    float* red = reinterpret_cast<float*>(smem + C::NST * C::STAGE);
+    float2* red = reinterpret_cast<float2*>(smem + C::NST * C::STAGE);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGE + C::RED);
     uint64_t* empty = full + C::NST;
     __shared__ int s_last;
@@ -96,46 +219,53 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
     const Plan pl = *a.plan;
     const int nb = a.ntn / 8;
     const int S = GATEUP ? pl.S_gu : pl.S_d;
-    const int kqs = (a.kt / RB) / S;                        // stages per item
-    const long long items = (long long) pl.J * nb * S;
+    const int kqs = (a.kt / RB) / S;                        // stages per item and matrix
+    const int items = pl.J * nb * S;                        // < 2^31: J <= rows + 1, nb <= 64, S <= 64
 
     if (warp == NCW)
     {
         // ---------------- producer ----------------
         if (lane != 0) return;
-        long long it = 0;
-        for (long long item = blockIdx.x; item < items && !s_abort; item += gridDim.x)
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        for (int item = blockIdx.x; item < items && !s_abort; item += gridDim.x)
         {
-            const int ks = (int) (item % S);
-            const long long jn = item / S;
-            const int nbi = (int) (jn % nb), j = (int) (jn / nb);
+            const int ks = item % S;
+            const int jn = item / S;
+            const int nbi = jn % nb, j = jn / nb;
             const int4 job = a.jobs[j];
-            const CUtensorMap* m0 = a.tmaps + job.x * 3 + a.proj0;
-            const uint32_t bytes = (uint32_t) (C::MAT0 + C::MAT1 + NMAT * job.z * 256);
-            for (int q = 0; q < kqs; ++q, ++it)
+            for (int m = 0; m < NMAT && !s_abort; ++m)
             {
-                const int s = (int) (it % C::NST);
-                const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
-                if (!s_abort && !mbar_wait_bounded(&empty[s], ph ^ 1u)) { atomicOr(a.err, ERR_TIMEOUT_EMPTY); s_abort = 1; }
-                if (s_abort) break;
-                const int kr = (ks * kqs + q) * RB;
-                uint8_t* st = ring + s * C::STAGE;
-                mbar_arrive_expect_tx(&full[s], bytes);
-                // the stage's RB k-tile rows x 8 tiles of each matrix: one tensor copy (x in 32-bit words)
-                tma_load_2d(st, m0, nbi * 8 * C::TB0 / 4, kr, &full[s]);
-                if (NMAT > 1) tma_load_2d(st + C::MAT0, m0 + 1, nbi * 8 * C::TB1 / 4, kr, &full[s]);
-                uint8_t* xs = st + C::MAT0 + C::MAT1;
-                for (int i = 0; i < job.z; ++i)
-                    bulk_g2s(xs + i * XROW, a.xin0 + (size_t) (job.y + i) * a.kdim + kr * 16, 256, &full[s]);
-                if (NMAT > 1)
+                const CUtensorMap* map = a.tmaps + job.x * 3 + a.proj0 + m;
+                const int tb = m ? C::TB1 : C::TB0, rowb = m ? C::ROW1 : C::ROW0;
+                const __half* xin = m ? a.xin1 : a.xin0;
+                const uint32_t bytes = (uint32_t) (RB * rowb + job.z * XROW);
+                for (int q = 0; q < kqs; ++q)
+                {
+                    if (!s_abort && !mbar_wait_bounded(&empty[s], ph ^ 1u)) { atomicOr(a.err, ERR_TIMEOUT_EMPTY); s_abort = 1; }
+                    if (s_abort) break;
+                    const int kr = (ks * kqs + q) * RB;
+                    uint8_t* st = ring + s * C::STAGE;
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    // the stage's RB k-tile rows x 8 tiles of the matrix: one tensor copy (x in 32-bit words)
+                    tma_load_2d(st, map, nbi * 8 * tb / 4, kr, &full[s]);
                     for (int i = 0; i < job.z; ++i)
-                        bulk_g2s(xs + C::XS + i * XROW, a.xin1 + (size_t) (job.y + i) * a.kdim + kr * 16, 256, &full[s]);
+                        bulk_g2s(st + C::MAT + i * XROW, xin + (size_t) (job.y + i) * a.kdim + kr * 16, XROW, &full[s]);
+                    ++issued;
+                    if (++s == C::NST) { s = 0; ph ^= 1u; }
+                }
             }
         }
-        // drain: every issued stage must have landed before the CTA may exit
-        const long long first = it > C::NST ? it - C::NST : 0;
-        for (long long k = first; k < it; ++k)
-            if (!mbar_wait_bounded(&full[k % C::NST], (uint32_t) ((k / C::NST) & 1))) { atomicOr(a.err, ERR_TIMEOUT_FULL); break; }
+        // drain: every issued stage must have landed before the CTA may exit (the last min(issued, NST) stages, in
+        // issue order, each with the phase it was issued in)
+        const int nd = issued < C::NST ? issued : C::NST;
+        int ds = s - nd, dph = (int) ph;
+        if (ds < 0) { ds += C::NST; dph ^= 1; }
+        for (int k = 0; k < nd; ++k)
+        {
+            if (!mbar_wait_bounded(&full[ds], (uint32_t) dph)) { atomicOr(a.err, ERR_TIMEOUT_FULL); break; }
+            if (++ds == C::NST) { ds = 0; dph ^= 1; }
+        }
         return;
     }
 
@@ -146,81 +276,33 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
     L1.init(lane);
     OnesFrag ones;
     ones.init(lane);
-    const int g = lane >> 2, tq = lane & 3;
-    // per-lane offsets inside a stage: this warp's tile of k-row 0 and this lane's B-fragment words
-    const int t0_off = warp * C::TB0, t1_off = C::MAT0 + warp * C::TB1;
-    const int x_off = C::MAT0 + C::MAT1 + g * XROW + tq * 4;
-    long long it = 0;
-    for (long long item = blockIdx.x; item < items; item += gridDim.x)
+    int s = 0;
+    uint32_t ph = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x)
     {
-        const long long jn = item / S;
-        const int nbi = (int) (jn % nb), j = (int) (jn / nb);
+        const int jn = item / S;
+        const int nbi = jn % nb, j = jn / nb;
         const int4 job = a.jobs[j];
-        // Accumulation: one tensor-core chain per 128-input block (a pipeline stage), then the block sum is added into
-        // a (hi, lo) fp32 pair with Fast2Sum, so rounding errors do not grow with the chain length.
-        float acc[NMAT][4], lo[NMAT][4];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int v = 0; v < 4; ++v) acc[m][v] = lo[m][v] = 0.0f;
-
-        for (int q = 0; q < kqs; ++q, ++it)
+        switch (job.z)
         {
-            const int s = (int) (it % C::NST);
-            const uint32_t ph = (uint32_t) ((it / C::NST) & 1);
-            if (!s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(a.err, ERR_TIMEOUT_FULL); s_abort = 1; }
-            const uint8_t* st = ring + s * C::STAGE;
-            float blk[NMAT][4];
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) blk[m][0] = blk[m][1] = blk[m][2] = blk[m][3] = 0.0f;
-#pragma unroll
-            for (int r = 0; r < RB; ++r)
-            {
-                uint32_t af[4];
-                decode_frag_tc<K0>(st + t0_off + r * C::ROW0, L0, ones, af);
-                mma16816(blk[0], af, lds32(st + x_off + r * 32), lds32(st + x_off + r * 32 + 16));
-                if (NMAT > 1)
-                {
-                    uint32_t bf[4];
-                    decode_frag_tc<K1>(st + t1_off + r * C::ROW1, L1, ones, bf);
-                    mma16816(blk[NMAT - 1], bf, lds32(st + x_off + C::XS + r * 32), lds32(st + x_off + C::XS + r * 32 + 16));
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
-                {
-                    const float sum = __fadd_rn(acc[m][v], blk[m][v]);
-                    const float big = fabsf(acc[m][v]) >= fabsf(blk[m][v]) ? acc[m][v] : blk[m][v];
-                    const float small = fabsf(acc[m][v]) >= fabsf(blk[m][v]) ? blk[m][v] : acc[m][v];
-                    lo[m][v] = __fadd_rn(lo[m][v], __fsub_rn(small, __fsub_rn(sum, big)));
-                    acc[m][v] = sum;
-                }
-        }
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int v = 0; v < 4; ++v) acc[m][v] = __fadd_rn(acc[m][v], lo[m][v]);
-
-        // ---- epilogue: fragments -> red[mat][token][128] ----
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-        {
-            float* rm = red + m * MAXM * 128;
-            const int o = warp * 16 + g;
-            rm[(2 * tq) * 128 + o] = acc[m][0];
-            rm[(2 * tq + 1) * 128 + o] = acc[m][1];
-            rm[(2 * tq) * 128 + o + 8] = acc[m][2];
-            rm[(2 * tq + 1) * 128 + o + 8] = acc[m][3];
+            case 1: item_consume<K0, K1, NMAT, 1>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+            case 2: item_consume<K0, K1, NMAT, 2>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+            case 3: item_consume<K0, K1, NMAT, 3>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+#if GLMX_EXACT_MAXM > 4
+            case 4: item_consume<K0, K1, NMAT, 4>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+            case 5: item_consume<K0, K1, NMAT, 5>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+            case 6: item_consume<K0, K1, NMAT, 6>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+            case 7: item_consume<K0, K1, NMAT, 7>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
+#endif
+            default: item_consume<K0, K1, NMAT, EXACT_MAXM>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
         }
         consumer_sync();
         if (S > 1)
         {
-            constexpr int NV = NMAT * MAXM * 128;
-            float* part = a.partials + (size_t) item * NV;
+            // split-K: each piece stores its (hi, lo) pairs; the last to arrive adds them in split order (TwoSum on the
+            // hi parts, lo parts added), so the split does not round the partial sums to fp32
+            constexpr int NV = NMAT * EXACT_MAXM * 128;
+            float2* part = a.partials + (size_t) item * NV;
             for (int i = tid; i < NV; i += NCW * 32) __stcg(part + i, red[i]);
             __threadfence();
             consumer_sync();
@@ -232,12 +314,20 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
             consumer_sync();
             if (!s_last) continue;
             __threadfence();
-            const float* p0 = a.partials + (size_t) (jn * S) * NV;
+            const float2* p0 = a.partials + (size_t) jn * S * NV;
             for (int i = tid; i < NV; i += NCW * 32)
             {
-                float v = 0.0f;
-                for (int k = 0; k < S; ++k) v += __ldcg(p0 + (size_t) k * NV + i);
-                red[i] = v;
+                float h = 0.0f, l = 0.0f;
+                for (int k = 0; k < S; ++k)
+                {
+                    const float2 v = __ldcg(p0 + (size_t) k * NV + i);
+                    const float sum = __fadd_rn(h, v.x);
+                    const float bb = __fsub_rn(sum, h);
+                    const float e = __fadd_rn(__fsub_rn(h, __fsub_rn(sum, bb)), __fsub_rn(v.x, bb));
+                    l = __fadd_rn(__fadd_rn(l, v.y), e);
+                    h = sum;
+                }
+                red[i] = make_float2(h, l);
             }
             consumer_sync();
         }
@@ -252,8 +342,9 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
                 {
-                    gv[q] = r16(red[i * 128 + lane + 32 * q]);
-                    uv[q] = r16(red[MAXM * 128 + i * 128 + lane + 32 * q]);
+                    const float2 gp = red[i * 128 + lane + 32 * q], up = red[EXACT_MAXM * 128 + i * 128 + lane + 32 * q];
+                    gv[q] = r16(__fadd_rn(gp.x, gp.y));
+                    uv[q] = r16(__fadd_rn(up.x, up.y));
                 }
                 had128_warp(gv, lane);
                 had128_warp(uv, lane);
@@ -270,15 +361,19 @@ __global__ void __launch_bounds__(NTHR, CTAS_PER_SM) gemv_kernel(GemvArgs a)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
                 {
-                    const int c = lane + 32 * q;     // stored in PERM16 order inside each 16-row tile (decode_frag_tc)
-                    a.xd[(size_t) row * a.ndim + nbi * 128 + (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(av[q], HAD));
+                    const int c = lane + 32 * q;     // the down GEMV reads its input in the gemv_xpos lane order
+                    a.xd[(size_t) row * a.ndim + nbi * 128 + gemv_xpos(c)] = __float2half_rn(__fmul_rn(av[q], HAD));
                 }
             }
             else
             {
                 float yv[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) yv[q] = r16(red[i * 128 + lane + 32 * q]);
+                for (int q = 0; q < 4; ++q)
+                {
+                    const float2 yp = red[i * 128 + lane + 32 * q];
+                    yv[q] = r16(__fadd_rn(yp.x, yp.y));
+                }
                 had128_warp(yv, lane);
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
@@ -346,8 +441,8 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
 #pragma unroll
         for (int q = 0; q < 4; ++q)
         {
-            const int c = lane + 32 * q;         // GEMV: PERM16 order inside each 16-row tile (decode_frag_tc)
-            out[a.natural ? c : (c & ~15) + perm16_inv(c & 15)] = __float2half_rn(__fmul_rn(v[q], HAD));
+            const int c = lane + 32 * q;         // GEMV: the lane order of gemv_xpos
+            out[a.natural ? c : gemv_xpos(c)] = __float2half_rn(__fmul_rn(v[q], HAD));
         }
     }
 }
@@ -524,7 +619,6 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     const int n = ntok * topk;
     const int rows = n + (L.has_shared ? ntok : 0);
     const int jobs = rows + 1;                       // each job holds >= 1 row
-    const int nmax = (L.H > L.I ? L.H : L.I);
     w.rows_max = rows; w.jobs_max = jobs; w.part_slots = 2 * grid_ctas;
     size_t o = 0;
     auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + (bytes ? bytes : 1)); return at; };
@@ -544,7 +638,7 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.xu = take(sizeof(__half) * (size_t) rows * L.H);
     w.xd = take(sizeof(__half) * (size_t) rows * L.I);
     w.yrow = take(sizeof(float) * (size_t) rows * L.H);
-    w.partials = take(sizeof(float) * (size_t) w.part_slots * 2 * MAXM * 128 + 0 * nmax);
+    w.partials = take(sizeof(float2) * (size_t) w.part_slots * 2 * EXACT_MAXM * 128);   // EXACT split-K (hi, lo) pairs
     // raw fp32 gate/up outputs (I16 GEMV: one slice; prefill GEMM: one slice per K split)
     w.yraw_gu = take(sizeof(float) * (size_t) PF_KSPLIT * rows * 2 * L.I);
     // I16 mode (decode-sized calls only): jobs of <= I16_MAXM rows of one expert: at most rows/4 + one partial job per
@@ -604,7 +698,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
         g.trellis = L.d_trellis;
         g.tmaps = L.d_tmaps;
         g.err = reinterpret_cast<int*>(ws + lay.err);
-        g.partials = reinterpret_cast<float*>(ws + lay.partials);
+        g.partials = reinterpret_cast<float2*>(ws + lay.partials);
         g.act_limit = L.act_limit;
         // gate + up
         g.proj0 = 0; g.kt = L.H / 16; g.ntn = L.I / 16; g.kdim = L.H; g.ndim = L.I;

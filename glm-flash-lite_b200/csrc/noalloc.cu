@@ -25,17 +25,11 @@ constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of the scratch on the current device, resolved once per device (this is the set-up the first call
-// on each device performs; the symbol lookup may load this module, so that first call belongs outside stream capture).
-int scratch_for_current_device(void** ptr)
+// Device address of the scratch on device `dev`, resolved once per device (this is the set-up the first call on each
+// device performs; the symbol lookup may load this module on that device, so that first call belongs outside stream
+// capture). The caller has checked that `dev` is the current device.
+int scratch_for_device(int dev, void** ptr)
 {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-    {
-        glmx::set_error(std::string("glmx_moe_forward_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
-        return GLMX_E_CUDA;
-    }
     if (dev < 0 || dev >= kMaxDevices)
     {
         glmx::set_error("glmx_moe_forward_noalloc: device index out of range");
@@ -45,7 +39,7 @@ int scratch_for_current_device(void** ptr)
     if (!g_scratch_ptr[dev])
     {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p)
         {
             glmx::set_error(std::string("glmx_moe_forward_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
@@ -54,6 +48,27 @@ int scratch_for_current_device(void** ptr)
         g_scratch_ptr[dev] = p;
     }
     *ptr = g_scratch_ptr[dev];
+    return GLMX_OK;
+}
+
+// The layer's device, which must be the current device (checked before anything touches the scratch, so a call on
+// the wrong device neither loads the module there nor resolves its array).
+int layer_device(const glmx_layer* layer, const char* who, int* dev)
+{
+    const int ldev = glmx_layer_device(layer);
+    int cur = -1;
+    const cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess)
+    {
+        glmx::set_error(std::string(who) + ": cudaGetDevice: " + cudaGetErrorString(e));
+        return GLMX_E_CUDA;
+    }
+    if (ldev < 0 || cur != ldev)
+    {
+        glmx::set_error(std::string(who) + ": current device differs from the layer's device");
+        return GLMX_E_ARG;
+    }
+    *dev = ldev;
     return GLMX_OK;
 }
 
@@ -82,9 +97,28 @@ extern "C" int glmx_moe_forward_noalloc(const glmx_layer* layer, const void* x, 
                         "); split the batch or call glmx_moe_forward with a caller-owned workspace");
         return GLMX_E_WORKSPACE;
     }
+    int dev = -1;
+    int rc = layer_device(layer, "glmx_moe_forward_noalloc", &dev);
+    if (rc != GLMX_OK) return rc;
     void* scratch = nullptr;
-    const int rc = scratch_for_current_device(&scratch);
+    rc = scratch_for_device(dev, &scratch);
     if (rc != GLMX_OK) return rc;
     return glmx_moe_forward(layer, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, out, out_dtype, accumulate,
                             scratch, (size_t) GLMX_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int glmx_check_noalloc(const glmx_layer* layer, int ntok, int topk, void* stream, int* flags)
+{
+    if (!layer || ntok < 0 || topk < 0)
+    {
+        glmx::set_error("glmx_check_noalloc: bad argument");
+        return GLMX_E_ARG;
+    }
+    int dev = -1;
+    int rc = layer_device(layer, "glmx_check_noalloc", &dev);
+    if (rc != GLMX_OK) return rc;
+    void* scratch = nullptr;
+    rc = scratch_for_device(dev, &scratch);
+    if (rc != GLMX_OK) return rc;
+    return glmx_check(layer, ntok, topk, scratch, stream, flags);
 }

@@ -84,6 +84,9 @@ GLMX_API const char* glmx_last_error(void);
 GLMX_API int glmx_layer_create(const glmx_layer_desc* desc, glmx_layer** out);
 /* The per-layer part of tier_stop (kernels/cpu_avx2/ft_tier_ext.cpp:837): frees the layer's device table and tensor maps. */
 GLMX_API int glmx_layer_destroy(glmx_layer* layer);
+/* No counterpart (the reference's tier is one process-wide CPU pool): the CUDA device index the layer was created on
+ * (the current device at glmx_layer_create), or GLMX_E_ARG for a null layer. */
+GLMX_API int glmx_layer_device(const glmx_layer* layer);
 /* tier_set_act_limit (kernels/cpu_avx2/ft_tier_ext.cpp:635) */
 GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
 
@@ -207,7 +210,8 @@ GLMX_API int glmx_router(const void* z, int z_dtype, int ntok, int hidden, const
                          float* logits, void* sel, int sel_dtype, void* w, int w_dtype, void* stream);
 
 /* Size of the scratch built into the library for glmx_moe_forward_noalloc: 48 MiB, which holds the workspace of up
- * to 8 tokens x top-8 (+ a shared expert) at H = 6144, I = 1536, in either mode. */
+ * to 8 tokens x top-8 (+ a shared expert) at H = 6144, I = 1536, in either mode, on a GPU of up to 148 SMs (B200; the
+ * split-K partial sums of the workspace grow with the SM count, so a part with more SMs may take fewer tokens). */
 #define GLMX_NOALLOC_SCRATCH_BYTES (48u << 20)
 
 /* glmx_moe_forward without a workspace argument, for callers that cannot allocate device memory for one: a host in
@@ -222,10 +226,15 @@ GLMX_API int glmx_router(const void* z, int z_dtype, int ntok, int hidden, const
  *     load the library's device code); make that first call before any stream capture.
  *   - All calls on one device share the one scratch: calls that overlap in time (different streams, or host threads
  *     whose work is in flight together) race and corrupt each other's results. Calls queued on one stream are safe.
- *   - Device-side error flags of these calls stay in the library's scratch (no workspace to hand to glmx_check). */
+ *   - Device-side error flags of these calls stay in the library's scratch: glmx_check_noalloc reads them. */
 GLMX_API int glmx_moe_forward_noalloc(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
                      int sel_dtype, const void* w, int w_dtype, int topk, int mode, void* out, int out_dtype, int accumulate,
                      void* stream);
+
+/* glmx_check for glmx_moe_forward_noalloc: synchronises `stream` and reads the device error word of the built-in
+ * scratch for a call of (ntok, topk) (the same word glmx_check reads in a caller's workspace). No counterpart in the
+ * reference. The layer's device must be current. */
+GLMX_API int glmx_check_noalloc(const glmx_layer* layer, int ntok, int topk, void* stream, int* flags);
 
 #ifdef __cplusplus
 }

@@ -15,6 +15,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libftoracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libftref.so")
+# the reference tree beside the repository (a checkout of nkeilar/glm-flash-lite next to this one); REF_KDIR overrides
+REF_KDIR_DEFAULT = os.path.normpath(os.path.join(HERE, "..", "..", "reference", "kernels", "cpu_avx2"))
 
 _P = C.c_void_p
 _I = C.c_int
@@ -24,7 +26,7 @@ _F = C.c_float
 def build(ref: bool = True) -> None:
     """Build the restatement, and the reference shim when the reference tree exists."""
     targets = ["oracle"]
-    if ref and os.path.isdir(os.environ.get("REF_KDIR", "/root/reference/kernels/cpu_avx2")):
+    if ref and os.path.isdir(os.environ.get("REF_KDIR", REF_KDIR_DEFAULT)):
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
@@ -307,6 +309,35 @@ def with_shared_routes(sel: np.ndarray, w: np.ndarray, E: int):
     sel2 = np.concatenate([sel, np.full((ntok, 1), E, np.int32)], axis=1)
     w2 = np.concatenate([w, np.ones((ntok, 1), np.float32)], axis=1)
     return sel2, w2
+
+
+# EXACT-mode parity rule (one rule for the tests and the smoke check). The north-star bar is max-abs <= 2e-3 x RMS of
+# the output; at H=6144 the reference's own fp32 kernels sit above it (its fp16 rounding points turn accumulation-order
+# differences into 1-ulp flips), so the bar is the larger of 2e-3 and EXACT_SLACK x the distance of the reference's more
+# accurate schedule (moe_forward_band, ft_core.h:1617-1651) from the fp64 restatement on the same inputs; rel-RMS must
+# be within EXACT_SLACK of the reference's own EXACT kernels' (the larger of moe_forward and moe_forward_band), with a
+# floor of EXACT_RELRMS_FLOOR for inputs where both happen to be almost exact. The slack covers single 1-ulp flips at
+# an fp16 rounding point, which dominate both metrics on any one input; averaged over many inputs the tests require
+# the GPU to be at least as close to the fp64 restatement as the band kernel.
+EXACT_MAXABS = 2e-3
+EXACT_SLACK = 1.25
+EXACT_RELRMS_FLOOR = 5e-5
+
+
+def exact_bars(oracle_fp64: np.ndarray, ref_fp32: np.ndarray | None = None, band_fp32: np.ndarray | None = None):
+    """(max-abs bar, rel-RMS bar) of the EXACT-mode rule for one input, from the reference's own outputs on it
+    (either may be None: the bar then rests on the other, or on the north-star values when both are absent)."""
+    bar_mx, bar_rr = EXACT_MAXABS, EXACT_RELRMS_FLOOR
+    refs = [r for r in (ref_fp32, band_fp32) if r is not None]
+    if band_fp32 is not None:
+        bar_mx = max(bar_mx, EXACT_SLACK * rel_err(band_fp32, oracle_fp64)[0])
+    elif ref_fp32 is not None:
+        bar_mx = max(bar_mx, EXACT_SLACK * rel_err(ref_fp32, oracle_fp64)[0])
+    if refs:
+        bar_rr = max([bar_rr] + [EXACT_SLACK * rel_err(r, oracle_fp64)[1] for r in refs])
+    else:
+        bar_rr = 5e-4
+    return bar_mx, bar_rr
 
 
 def rel_err(a: np.ndarray, ref: np.ndarray):

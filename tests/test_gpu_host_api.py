@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_exact_mode
+from conftest import assert_exact_mode, reference_outputs
 
 pytestmark = pytest.mark.gpu
 
@@ -39,7 +39,8 @@ def test_tier_forward_matches_oracle(oracle):
             assert got.device.type == "cpu" and got.dtype == torch.float32
             np.testing.assert_array_equal(got.numpy(), want)
         got = tier.tier_forward(0, xt, st, wt, 1).numpy()
-        assert_exact_mode(got, oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1), None, "tier EXACT")
+        assert_exact_mode(got, oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1),
+                          *reference_outputs(bank, x, sel, w), label="tier EXACT")
         assert tier.tier_stats()[0] == 3
     finally:
         tier.tier_reset()

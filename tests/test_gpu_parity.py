@@ -3,7 +3,7 @@ north-star bar (max-abs <= 2e-3 x RMS of the output)."""
 import numpy as np
 import pytest
 
-from conftest import TOL_MAXABS_REL_RMS, assert_exact_mode, golden_bank, load_golden, parity, reference_or_none
+from conftest import TOL_MAXABS_REL_RMS, assert_exact_mode, golden_bank, load_golden, parity, reference_outputs
 
 pytestmark = pytest.mark.gpu
 
@@ -80,7 +80,7 @@ def test_route_bit_exact(oracle, dev, ntok, topk, E):
 @pytest.mark.parametrize("name", ["moe_small", "moe_baseline"])
 def test_exact_layer_golden(oracle, dev, name):
     """EXACT mode on the golden reference layers (inputs of the reference's A/B harness) vs the fp64 oracle, judged
-    against the reference's own fp32 EXACT kernel output stored in the fixture."""
+    against the reference's own fp32 EXACT kernels' outputs stored in the fixture (moe_forward and its band form)."""
     d = load_golden(name)
     bank = golden_bank(d)
     layer = _layer(bank, dev)
@@ -90,13 +90,13 @@ def test_exact_layer_golden(oracle, dev, name):
         got = out.cpu().numpy()
         assert layer.check_device(*sel.shape) == 0
         want = oracle.moe_forward(bank, x, sel, w, mode=1)
-        assert_exact_mode(got, want, d[f"{tag}_exact"], label=f"{name}/{tag}")
+        assert_exact_mode(got, want, d[f"{tag}_exact"], d[f"{tag}_band_exact"], label=f"{name}/{tag}")
 
 
 @pytest.mark.parametrize("ntok", [1, 4])
 def test_exact_layer_baseline_geometry(oracle, dev, ntok):
     """EXACT mode at BASELINE configs[1] shape (H=6144, I=1536, K=3, top-8 sigmoid router), 24 routed + shared,
-    against the reference's fp32 EXACT moe_forward run live on the same inputs."""
+    against the reference's fp32 EXACT kernels (moe_forward, moe_forward_band) run live on the same inputs."""
     from glmx import synth
     from oracle.oracle import with_shared_routes
     E = 24
@@ -107,12 +107,8 @@ def test_exact_layer_baseline_geometry(oracle, dev, ntok):
     out = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(sel).to(dev), torch.from_numpy(w).to(dev), mode=1)
     got = out.cpu().numpy()
     want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1)
-    ref = reference_or_none()
-    ref_out = None
-    if ref is not None:
-        ref_out = ref.moe_forward(ref.layer(bank, with_shared=True), x.astype(np.float32), *with_shared_routes(sel, w, E), mode=1)
-        ref.stop_pool()
-    assert_exact_mode(got, want, ref_out, label=f"baseline ntok={ntok}")
+    ref_out, band_out = reference_outputs(bank, x, sel, w)
+    assert_exact_mode(got, want, ref_out, band_out, label=f"baseline ntok={ntok}")
 
 
 @pytest.mark.parametrize("bits", [(2, 2, 2), (4, 4, 4), (4, 4, 2), (2, 3, 4)])
@@ -128,7 +124,7 @@ def test_exact_layer_mixed_bitrate(oracle, dev, bits):
     got = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(sel).to(dev), torch.from_numpy(w).to(dev),
                         mode=1).cpu().numpy()
     want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1)
-    assert_exact_mode(got, want, None, label=str(bits))
+    assert_exact_mode(got, want, label=str(bits), floor=True)
 
 
 def test_accumulate_and_fp16_out(oracle, dev):

@@ -3,7 +3,7 @@ Jobs of up to 128 rows per expert; ragged last jobs, the shared expert's rows, m
 import numpy as np
 import pytest
 
-from conftest import TOL_MAXABS_REL_RMS, assert_exact_mode, parity, reference_or_none
+from conftest import TOL_MAXABS_REL_RMS, assert_exact_mode, parity, reference_outputs
 
 pytestmark = pytest.mark.gpu
 
@@ -14,24 +14,6 @@ torch = pytest.importorskip("torch")
 def dev():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     return torch.device("cuda", 0)
-
-
-def _reference_fp32(bank, x, sel, w):
-    """The reference's own fp32 EXACT kernel (moe_forward mode 1, the one tier_forward runs) on the same inputs: it
-    sets the EXACT-mode bar where it exists (K=3 banks, oracle/_ref built); None otherwise (the fixed floor applies).
-    Its fp32 summation order is as far from the fp64 restatement as the tensor-core GEMM (max-abs 3.9-4.6e-3, rel-RMS
-    3.5e-4 x RMS at H=6144 over three seeds); the reference's band schedule is closer (2.5e-4) and so is the GEMV path."""
-    ref = reference_or_none()
-    if ref is None or tuple(bank.bits) != (3, 3, 3):
-        return None
-    import os
-    from oracle.oracle import with_shared_routes
-    ref.start_pool(max(1, min(8, len(os.sched_getaffinity(0)) - 1)))
-    try:
-        return ref.moe_forward(ref.layer(bank, with_shared=True), x.astype(np.float32),
-                               *with_shared_routes(sel, w, bank.E), mode=1, band=False)
-    finally:
-        ref.stop_pool()
 
 
 def _run(layer, x, sel, w, mode, dev):
@@ -56,7 +38,8 @@ def test_prefill_gemm_vs_oracle(oracle, dev, H, I, E, ntok, topk, bits):
     got = _run(layer, x, sel, w, _lib.MODE_EXACT | _lib.PATH_GEMM, dev)
     want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1)
     assert np.isfinite(got).all()
-    assert_exact_mode(got, want, _reference_fp32(bank, x, sel, w), f"prefill {H}x{I} bits {bits}")
+    assert_exact_mode(got, want, *reference_outputs(bank, x, sel, w), label=f"prefill {H}x{I} bits {bits}",
+                      floor=tuple(bits) != (3, 3, 3))
     # the GEMV path on the same inputs: a different fp32 accumulation order, so only fp16 rounding flips differ
     gemv = _run(layer, x, sel, w, _lib.MODE_EXACT | _lib.PATH_GEMV, dev)
     mx, rr = parity(got, gemv)
@@ -75,7 +58,7 @@ def test_prefill_baseline_geometry(oracle, dev):
     w = rng.random((ntok, topk)).astype(np.float32)
     got = _run(layer, x, sel, w, _lib.MODE_EXACT | _lib.PATH_GEMM, dev)
     want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1)
-    assert_exact_mode(got, want, _reference_fp32(bank, x, sel, w), "prefill baseline geometry")
+    assert_exact_mode(got, want, *reference_outputs(bank, x, sel, w), label="prefill baseline geometry")
 
 
 def test_prefill_auto_path_and_accumulate(oracle, dev):
