@@ -506,16 +506,17 @@ def run_prefill(args, dev):
 
 
 def run_expert_parallel(args, rank, world, dev, dist):
-    """N > 1: configs[3]'s sharding on one layer. The 288 routed experts are split contiguously over the ranks
-    (288/N each), the shared expert is replicated; the global decode batch (args.batch, 64) is split over the ranks
-    (64/N tokens each, the tokens a data-parallel attention stage would own). A step = one expert-parallel layer
-    call (all-gather dispatch, local shard + the shared expert on the own rows in one layer call, reduce-scatter
-    return).
+    """Expert parallelism over N ranks (configs[3]'s sharding) and, with --layers L, configs[3]'s stack of L MoE layers.
+    The 288 routed experts of each layer are split contiguously over the ranks (288/N each), the shared expert is
+    replicated; the global decode batch (args.batch, 64) is split over the ranks (64/N tokens each, the tokens a
+    data-parallel attention stage would own). A step = the L layers in sequence, layer l + 1 taking layer l's fp32
+    output as its input (fresh uniform top-8 routing per layer); with N = 1 each layer is a plain single-GPU layer call.
     Strong scaling: the total work per step is the N=1 workload. Device time, max over ranks."""
     import torch
     from glmx import MoELayer, ep
 
     Bg = args.batch
+    L = args.layers
     if Bg % world or E % world:
         raise SystemExit(f"batch {Bg} and experts {E} must divide by {world}")
     b = Bg // world
@@ -534,97 +535,139 @@ def run_expert_parallel(args, rank, world, dev, dist):
                for m in (I, I, H)]
         return tr, ptrs, suh, svh
 
-    tr, ptrs, suh, svh = bank_of(n + 1)          # the shard's n experts + the shared expert (local id n)
-    local = MoELayer(H, I, n + 1, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev)
-    layer = ep.ExpertParallelLayer(local, first, n, has_shared=True, E=E, peer=args.peer)
+    layers = []
+    for l in range(L):
+        tr, ptrs, suh, svh = bank_of(n + 1)      # the shard's n experts + the shared expert (local id n / entry n)
+        if world == 1:
+            layers.append(MoELayer(H, I, n, ptrs, suh, svh, has_shared=True, keep=[tr], device=dev))
+        else:
+            local = MoELayer(H, I, n + 1, ptrs, suh, svh, has_shared=False, keep=[tr], device=dev)
+            layers.append(ep.ExpertParallelLayer(local, first, n, has_shared=True, E=E, peer=args.peer,
+                                                 exchange=args.exchange))
+    resident = L * (n + 1) * (EXPERT_BYTES_K3 + SCALE_BYTES)
     stream = torch.cuda.current_stream(dev)
     pk, pk_kind = peaks()
 
-    routes = make_routes(Bg, 1000)                         # the global routing, the same on every rank
-    sel = [torch.from_numpy(np.ascontiguousarray(s[rank * b:(rank + 1) * b])).to(dev) for s, _ in routes]
-    wts = [torch.from_numpy(np.ascontiguousarray(w[rank * b:(rank + 1) * b])).to(dev) for _, w in routes]
+    routes = [make_routes(Bg, 1000 + 17 * l) for l in range(L)]      # global routing per layer, the same on every rank
+    sel = [[torch.from_numpy(np.ascontiguousarray(s[rank * b:(rank + 1) * b])).to(dev) for s, _ in rl] for rl in routes]
+    wts = [[torch.from_numpy(np.ascontiguousarray(w[rank * b:(rank + 1) * b])).to(dev) for _, w in rl] for rl in routes]
     x = torch.randn((b, H), device=dev, generator=g).half()
-    out = torch.empty((b, H), dtype=torch.float32, device=dev)
-    # this shard's touched experts per step (+ the shared expert): its algorithmic bytes
-    touched = [int(np.unique(s[(s >= first) & (s < first + n)]).size) + 1 for s, _ in routes]
+    outs = [torch.empty((b, H), dtype=torch.float32, device=dev) for _ in range(L)]
+    # this shard's touched experts per step and layer (+ the shared expert): its algorithmic bytes
+    touched = [[int(np.unique(s[(s >= first) & (s < first + n)]).size) + 1 for s, _ in rl] for rl in routes]
+
+    def run_stack(i, x0):
+        h = x0
+        for l in range(L):
+            layers[l].forward(h, sel[l][i % ROUTE_POOL], wts[l][i % ROUTE_POOL], mode=args.mode, out=outs[l])
+            h = outs[l]
+        return h
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     def timed(step_fn, steps, warmup):
         for i in range(warmup):
             step_fn(i)
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        torch.cuda.synchronize(dev)
+        sync_all()
         t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for i in range(steps):
             step_fn(i)
         t1.record(stream)
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        t = torch.tensor([t0.elapsed_time(t1)], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def dev_step(i):
-        layer.forward(x, sel[i % ROUTE_POOL], wts[i % ROUTE_POOL], mode=args.mode, out=out)
+        sync_all()
+        return max_over_ranks(t0.elapsed_time(t1))
 
     clk_idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(rank)).split(",")[int(os.environ.get("LOCAL_RANK", "0"))]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else int(os.environ.get("LOCAL_RANK", "0"))
     with ClockSampler(clk_idx) as cs:
-        T_ms = timed(dev_step, args.steps, args.warmup)
+        T_ms = timed(lambda i: run_stack(i, x), args.steps, args.warmup)
     clocks = cs.summary()
     value = Bg * args.steps / (T_ms / 1e3)
-    my_bytes = sum(touched[i % ROUTE_POOL] for i in range(args.steps)) * (EXPERT_BYTES_K3 + SCALE_BYTES)
+    my_bytes = sum(touched[l][i % ROUTE_POOL] for l in range(L) for i in range(args.steps)) * (EXPERT_BYTES_K3 + SCALE_BYTES)
     tb = torch.tensor([float(my_bytes)], device=dev, dtype=torch.float64)
-    dist.all_reduce(tb)
+    if dist:
+        dist.all_reduce(tb)
     layer_gbs = float(tb.item()) / (T_ms / 1e3) / 1e9
 
-    # end to end: this rank's tokens from pinned host memory, result back to pinned host memory
+    # per-phase device times of layer 0's expert-parallel call (dispatch, compute, return), mean per call, max over ranks
+    phases = None
+    if world > 1 and not args.peer:
+        nph = max(10, min(args.steps, 50))
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nph)]
+        sync_all()
+        for i in range(nph):
+            layers[0].events = evs[i]
+            layers[0].forward(x, sel[0][i % ROUTE_POOL], wts[0][i % ROUTE_POOL], mode=args.mode, out=outs[0])
+        layers[0].events = None
+        sync_all()
+        ph = [sum(e[k].elapsed_time(e[k + 1]) for e in evs) / nph for k in range(3)]
+        phases = {name: max_over_ranks(v) for name, v in zip(("dispatch_ms", "compute_ms", "return_ms"), ph)}
+        phases["exchange"] = args.exchange
+
+    # end to end: this rank's tokens from pinned host memory, the last layer's result back to pinned host memory
     x_h = torch.randn((b, H)).half().pin_memory()
-    sel_h = [s.cpu().pin_memory() for s in sel]
-    w_h = [w.cpu().pin_memory() for w in wts]
     out_h = torch.empty((b, H), dtype=torch.float32).pin_memory()
-    x_d = torch.empty_like(x); s_d = torch.empty_like(sel[0]); w_d = torch.empty_like(wts[0])
+    x_d = torch.empty_like(x)
 
     def e2e_step(i):
-        x_d.copy_(x_h, non_blocking=True); s_d.copy_(sel_h[i % ROUTE_POOL], non_blocking=True)
-        w_d.copy_(w_h[i % ROUTE_POOL], non_blocking=True)
-        layer.forward(x_d, s_d, w_d, mode=args.mode, out=out)
-        out_h.copy_(out, non_blocking=True)
+        x_d.copy_(x_h, non_blocking=True)
+        out_h.copy_(run_stack(i, x_d), non_blocking=True)
 
     E_ms = timed(e2e_step, args.steps, args.warmup)
-    dist.barrier()
-    peer = layer.peer
-    peer_err = layer._ret.error_flags() if peer and layer._ret is not None else 0
-    layer.close()
-    del layer
-    dist.destroy_process_group()
+    peer_err = 0
+    if world > 1:
+        dist.barrier()
+        for ly in layers:
+            if ly.peer and ly._ret is not None:
+                peer_err |= ly._ret.error_flags()
+            ly.close()
+    del layers
+    if dist:
+        dist.destroy_process_group()
     if peer_err:
         raise RuntimeError(f"peer return error flags {peer_err}")
     if rank != 0:
         return
     peak = pk["hbm_gbs"] * world
+    ret = "peer memory, fused into the combine" if args.peer else \
+        ("NCCL all-to-all (per-destination rows)" if args.exchange == "a2a" else "NCCL reduce-scatter")
+    wl = (f"configs[3]: {L} MoE layers" if L > 1 else "configs[3] sharding on one configs[1] layer") + \
+        f", B={Bg} global decode tokens, {E} routed experts split {n}/GPU + replicated shared expert, H=6144, I=1536, K=3, top-8"
     line = {
-        "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None,
+        "metric": "moe_layer_decode_tok_per_s" if L == 1 else "moe_stack_decode_tok_per_s", "value": value, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
-        "config": {"workload": f"configs[3] sharding on one configs[1] layer: B={Bg} global decode tokens, {E} routed "
-                               f"experts split {n}/GPU + replicated shared expert, H=6144, I=1536, K=3, top-8",
-                   "batch": Bg, "tokens_per_gpu": b, "experts_per_gpu": n, "H": H, "I": I, "bits": 3, "topk": TOPK,
-                   "mode": {1: "EXACT", 2: "I16"}[args.mode], "parallelism": f"ep{world}",
-                   "return": "peer memory, fused into the combine" if peer else "NCCL reduce-scatter",
+        "config": {"workload": wl, "layers": L, "batch": Bg, "tokens_per_gpu": b, "experts_per_gpu": n, "H": H, "I": I,
+                   "bits": 3, "topk": TOPK, "mode": {1: "EXACT", 2: "I16"}[args.mode], "parallelism": f"ep{world}",
+                   "dispatch": "NCCL all-to-all of the rows each rank needs" if args.exchange == "a2a" and not args.peer
+                   else "NCCL all-gather", "return": ret,
                    "l2": "inputs larger than L2 (touched trellis per step > 126 MB)"},
+        "resident_expert_bytes_per_gpu": resident,
+        "ms_per_layer": T_ms / args.steps / L,
         "hbm_gbs_layer": layer_gbs,
-        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer step (all ranks)", "achieved": layer_gbs,
+        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel step (all ranks)", "achieved": layer_gbs,
                      "peak": peak, "unit": "GB/s", "frac": layer_gbs / peak, "peak_kind": pk_kind + f" x {world}",
                      "traffic": None},
+        "phases": phases,
         "cpu_baseline": None,
-        "e2e": {"value": Bg * args.steps / (E_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": world * (b * H * 2 + b * TOPK * 8),
+        "e2e": {"value": Bg * args.steps / (E_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": world * b * H * 2,
                 "d2h_bytes_per_step": world * b * H * 4},
-        # per step and rank: split + transform + gate/up + epilogue + down + combine (the shared expert rides along)
-        # (+ the owner's sum of the peer partials)
-        "gpu_launches": ((6 if args.mode == 2 else 5) + (1 if peer else 0)) * args.steps * world,
+        # per layer and rank: split + transform + gate/up (+ I16 epilogue) + down + combine of the routed call, the same
+        # for the shared expert's call (a2a), the pack (2) and unpack kernels; (+ the owner's sum of the peer partials)
+        "gpu_launches": (((6 if args.mode == 2 else 5) * (2 if args.exchange == "a2a" and world > 1 else 1)
+                          + (3 if args.exchange == "a2a" and world > 1 else 0) + (1 if args.peer else 0)) * L * args.steps * world),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -639,6 +682,10 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=1, help="configs[3]: a stack of this many MoE layers per step (42 = the "
+                    "full GLM-5.3 expert stack, about 129 GB at 1 GPU)")
+    ap.add_argument("--exchange", default="a2a", choices=["a2a", "allgather"], help="expert parallelism: per-destination "
+                    "all-to-all of the rows (a2a) or all-gather dispatch + reduce-scatter return")
     ap.add_argument("--peer", action="store_true", help="expert parallelism: return the partials with the combine's "
                     "peer-memory stores instead of NCCL's reduce-scatter")
     ap.add_argument("--sweep", default="1,8,32", help="extra decode batches measured (device time only)")
@@ -684,7 +731,7 @@ def main():
         if world > 1:
             raise SystemExit(f"the {args.workload} workload runs on one GPU")
         return {"prefill": run_prefill, "sweep": run_sweep, "router": run_router}[args.workload](args, dev)
-    if world > 1:
+    if world > 1 or args.layers > 1:
         return run_expert_parallel(args, rank, world, dev, dist)
 
     # ---- synthetic layer on the device: 289 experts x (gate|up|down) K=3 trellis + scales ----

@@ -86,6 +86,126 @@ __global__ void __launch_bounds__(256) ep_split_kernel(const int* route, int row
     wl[i] = wt;
 }
 
+// ---- expert-parallel dispatch / return as an all-to-all over the ranks ---------------------------------------------
+// ep_pack_kernel (one CTA): for each destination rank d (the owner of experts [d n, (d + 1) n)), the tokens with at least
+// one pick there, ascending: their order in the send buffer is (d, token). Writes counts[d], the send rows' token
+// index, their routing for d (local ids of d's shard, other picks -1 with weight 0, then the fp32 weight bits) and
+// pos[d][t] = send row of (d, t) or -1. total[0] = the number of send rows.
+constexpr int EP_T = 1024;
+
+__device__ int ep_block_scan(int v, int* warp_sums, int* total)
+{
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+    {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[wid] = x;
+    __syncthreads();
+    if (wid == 0)
+    {
+        int s = lane < (int) (blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+        {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const int before = (wid ? warp_sums[wid - 1] : 0) + x - v;
+    *total = warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return before;
+}
+
+__global__ void __launch_bounds__(EP_T) ep_pack_kernel(const int* sel, const float* w, int B, int k, int n, int world,
+                                                       int* counts, int* total, int* send_tok, int* send_route, int* pos)
+{
+    __shared__ int warp_sums[32];
+    int off = 0;
+    for (int d = 0; d < world; ++d)
+    {
+        const int lo = d * n, hi = lo + n;
+        for (int t0 = 0; t0 < B; t0 += EP_T)
+        {
+            const int t = t0 + threadIdx.x;
+            int has = 0;
+            if (t < B)
+                for (int j = 0; j < k; ++j)
+                {
+                    const int e = sel[(size_t) t * k + j];
+                    has |= (e >= lo && e < hi);
+                }
+            int cnt;
+            const int before = ep_block_scan(has, warp_sums, &cnt);
+            if (t < B)
+            {
+                const int r = off + before;
+                pos[(size_t) d * B + t] = has ? r : -1;
+                if (has)
+                {
+                    send_tok[r] = t;
+                    for (int j = 0; j < k; ++j)
+                    {
+                        const int e = sel[(size_t) t * k + j];
+                        const bool mine = e >= lo && e < hi;
+                        send_route[(size_t) r * 2 * k + j] = mine ? e - lo : -1;
+                        send_route[(size_t) r * 2 * k + k + j] = mine ? __float_as_int(w[(size_t) t * k + j]) : 0;
+                    }
+                }
+            }
+            off += cnt;
+        }
+        if (threadIdx.x == 0) counts[d] = off;          // end offset of d for now
+        __syncthreads();
+    }
+    // counts[d] so far holds the running end offset of d: turn it into the per-destination count
+    if (threadIdx.x == 0)
+    {
+        int prev = 0;
+        for (int d = 0; d < world; ++d) { const int end = counts[d]; counts[d] = end - prev; prev = end; }
+        *total = off;
+    }
+}
+
+// send_x[r] = x[send_tok[r]] for r < *total (rows of `row_bytes` bytes, 16-byte multiples)
+__global__ void __launch_bounds__(256) ep_gather_kernel(const uint4* x, int row16, const int* send_tok, const int* total,
+                                                        uint4* send_x, int max_rows)
+{
+    const int n = min(*total, max_rows);
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < (long long) n * row16;
+         i += (long long) gridDim.x * blockDim.x)
+    {
+        const int r = (int) (i / row16), c = (int) (i % row16);
+        send_x[i] = x[(size_t) send_tok[r] * row16 + c];
+    }
+}
+
+// out[t] += ret[pos[0][t]] + ... + ret[pos[world-1][t]] (rows present only), added in rank order
+__global__ void __launch_bounds__(256) ep_unpack_add_kernel(const float4* ret, const int* pos, int B, int world, int H4,
+                                                            float4* out)
+{
+    for (long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x; i < (long long) B * H4;
+         i += (long long) gridDim.x * blockDim.x)
+    {
+        const int t = (int) (i / H4), c = (int) (i % H4);
+        float4 v = out[i];
+        for (int d = 0; d < world; ++d)
+        {
+            const int r = pos[(size_t) d * B + t];
+            if (r < 0) continue;
+            const float4 u = ret[(size_t) r * H4 + c];
+            v.x = __fadd_rn(v.x, u.x); v.y = __fadd_rn(v.y, u.y); v.z = __fadd_rn(v.z, u.z); v.w = __fadd_rn(v.w, u.w);
+        }
+        out[i] = v;
+    }
+}
+
 int fail(int code, const std::string& msg)
 {
     set_error(msg);
@@ -127,6 +247,47 @@ extern "C" int glmx_ep_split(const int* route, int rows, int topk, int first, in
         route, rows, topk, first, n, shared ? 1 : 0, own_begin, own_end, loc, w);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(GLMX_E_CUDA, std::string("glmx_ep_split: launch: ") + cudaGetErrorString(e));
+    return GLMX_OK;
+}
+
+extern "C" int glmx_ep_pack(const int* sel, const float* w, int B, int topk, int experts_per_rank, int world, const void* x,
+                            int row_bytes, int* counts, int* total, int* send_tok, int* send_route, int* pos, void* send_x,
+                            void* stream)
+{
+    if (B < 0 || topk < 1 || topk > 64 || experts_per_rank < 1 || world < 1 || world > 64 || row_bytes <= 0 || row_bytes % 16 ||
+        !counts || !total || (B > 0 && (!sel || !w || !x || !send_tok || !send_route || !pos || !send_x)))
+        return fail(GLMX_E_ARG, "glmx_ep_pack: B >= 0, 1 <= topk <= 64, world in [1, 64], row_bytes a positive multiple of 16, "
+                                "non-null arrays");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send_x)) & 15u)
+        return fail(GLMX_E_ARG, "glmx_ep_pack: x and send_x must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ep_pack_kernel<<<1, EP_T, 0, st>>>(sel, w, B, topk, experts_per_rank, world, counts, total, send_tok, send_route, pos);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && B > 0)
+    {
+        const int row16 = row_bytes / 16;
+        const long long work = (long long) B * world * row16;
+        const unsigned grid = (unsigned) ((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
+        ep_gather_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), row16, send_tok, total, static_cast<uint4*>(send_x),
+                                               B * world);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return fail(GLMX_E_CUDA, std::string("glmx_ep_pack: launch: ") + cudaGetErrorString(e));
+    return GLMX_OK;
+}
+
+extern "C" int glmx_ep_unpack_add(const float* ret, const int* pos, int B, int world, int hidden, float* out, void* stream)
+{
+    if (B < 0 || world < 1 || world > 64 || hidden <= 0 || hidden % 4 || (B > 0 && (!ret || !pos || !out)))
+        return fail(GLMX_E_ARG, "glmx_ep_unpack_add: B >= 0, world in [1, 64], hidden a multiple of 4, non-null arrays");
+    if (B == 0) return GLMX_OK;
+    const int H4 = hidden / 4;
+    const long long work = (long long) B * H4;
+    const unsigned grid = (unsigned) ((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
+    ep_unpack_add_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const float4*>(ret), pos, B, world,
+                                                                                H4, reinterpret_cast<float4*>(out));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(GLMX_E_CUDA, std::string("glmx_ep_unpack_add: launch: ") + cudaGetErrorString(e));
     return GLMX_OK;
 }
 

@@ -45,7 +45,8 @@ EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_d
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
            "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc",
            "glmx_selftest_bounded_wait", "glmx_router", "glmx_moe_forward_peer", "glmx_peer_reduce", "glmx_ep_split", "glmx_ipc_alloc",
-           "glmx_ipc_free", "glmx_ipc_handle", "glmx_ipc_open", "glmx_ipc_close", "glmx_layer_device", "glmx_check_noalloc")
+           "glmx_ipc_free", "glmx_ipc_handle", "glmx_ipc_open", "glmx_ipc_close", "glmx_layer_device", "glmx_check_noalloc",
+           "glmx_ep_pack", "glmx_ep_unpack_add")
 IPC_HANDLE_BYTES = 64
 NOALLOC_SCRATCH_BYTES = 48 << 20
 ROUTER_MAX_EXPERTS = 512
@@ -85,6 +86,10 @@ def load(path: str = LIB_PATH):
     L.glmx_check.restype = _I
     L.glmx_moe_forward_noalloc.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I, _P]
     L.glmx_moe_forward_noalloc.restype = _I
+    L.glmx_ep_pack.argtypes = [_P, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]
+    L.glmx_ep_pack.restype = _I
+    L.glmx_ep_unpack_add.argtypes = [_P, _P, _I, _I, _I, _P, _P]
+    L.glmx_ep_unpack_add.restype = _I
     L.glmx_check_noalloc.argtypes = [_P, _I, _I, _P, C.POINTER(_I)]
     L.glmx_check_noalloc.restype = _I
     L.glmx_layer_device.argtypes = [_P]

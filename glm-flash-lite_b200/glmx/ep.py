@@ -2,7 +2,20 @@
 
 Rank r of N holds routed experts [r*E/N, (r+1)*E/N) and a copy of the shared expert, in ONE `MoELayer` of n + 1
 experts (the shard at local ids 0..n-1, the shared expert at local id n); every rank owns B tokens (the data-parallel
-part of the model gives each rank its own tokens). Per layer call:
+part of the model gives each rank its own tokens). Two exchanges.
+
+exchange="a2a" (the default): per destination, only the tokens with a pick there travel.
+
+  shared     the shared expert on the rank's own rows, on a side stream, while the exchange below is in flight
+  pack       glmx_ep_pack: per destination rank, its tokens (ascending), their rows and their picks in the
+             destination's local ids (one kernel; counts per destination)
+  dispatch   all-to-all of the counts, then (one host synchronisation for the split sizes) all-to-all of the rows and
+             of their routing
+  compute    one layer call over the received rows (this shard's picks only)
+  return     all-to-all of the fp32 results back to the token owners, in the order they were sent; glmx_ep_unpack_add
+             adds each token's returned rows in rank order onto the shared expert's output
+
+exchange="allgather" (and "peer"):
 
   dispatch   all-gather of the ranks' token rows x [B, H] and their routing (sel, w) [B, k] -> [N*B, ...]
   split      global ids -> local ids of this shard (others' ids masked to -1), plus one extra pick per row: the
@@ -137,7 +150,7 @@ class ExpertParallelLayer:
     """
 
     def __init__(self, local, first: int, n: int, has_shared: bool = True, group=None, E: int | None = None,
-                 peer: bool = False):
+                 peer: bool = False, exchange: str = "a2a"):
         self.local = local
         self.first, self.n, self.has_shared = int(first), int(n), bool(has_shared)
         self.group = group
@@ -151,7 +164,12 @@ class ExpertParallelLayer:
         if peer and not can:
             raise ValueError("the peer-memory return needs an NCCL group of GPU ranks and a MoELayer shard")
         self.peer = bool(peer)
+        self.exchange = "peer" if self.peer else exchange
+        if self.exchange not in ("a2a", "allgather", "peer"):
+            raise ValueError("exchange must be 'a2a', 'allgather' or 'peer'")
         self._ret = None
+        self._side = None
+        self.events = None        # optional 4 torch.cuda.Event: start, dispatch done, compute done, return done
 
     def close(self) -> None:
         """Release the peer mappings (collective: every rank calls it; before destroy_process_group)."""
@@ -178,7 +196,7 @@ class ExpertParallelLayer:
             self._bufs[key] = (s.contiguous(), own.to(torch.float32).reshape(NB, 1).contiguous())
         return self._bufs[key]
 
-    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = 2,
+    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = 1,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """x [B, H] (same B on every rank), sel [B, k] global expert ids (< 0 = masked), w [B, k] -> out [B, H] fp32."""
         B, H = x.shape
@@ -187,6 +205,9 @@ class ExpertParallelLayer:
         x = x.contiguous()
         sel = sel.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()
+        if self.exchange == "a2a":
+            return self._forward_a2a(x, sel, w, mode, out)
+        self._mark(0)
 
         # dispatch: token rows and routing of every rank
         xg = self._buf("xg", (N * B, H), x.dtype)
@@ -231,15 +252,126 @@ class ExpertParallelLayer:
             return out
 
         # compute: this shard's picks of all rows (+ shared on the own rows), one layer call
+        self._mark(1)
         partial = self._buf("partial", (N * B, H), torch.float32)
         self.local.forward(xg, loc, wl, mode=mode, out=partial, accumulate=False)
+        self._mark(2)
 
         # return: sum of the shards' partials, own rows
         _reduce_scatter(out, partial, self.group)
+        self._mark(3)
         return out
 
 
-def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0, peer: bool = False) -> ExpertParallelLayer:
+    # ---- all-to-all exchange ----------------------------------------------------------------------------------------
+    def _mark(self, i):
+        if self.events is not None and self.device.type == "cuda":
+            self.events[i].record(torch.cuda.current_stream(self.device))
+
+    def _pack(self, x, sel, w):
+        """(counts [N] int32, send_tok, send_route [., 2k] int32, pos [N, B] int32, send_x) in (destination, token) order."""
+        B, H = x.shape
+        k = sel.shape[1]
+        N, n = self.world, self.n
+        if self.device.type == "cuda" and hasattr(self.local, "lib"):
+            from . import _lib
+            from .layer import _stream_ptr
+            cnt = self._buf("a2a_counts", (N + 1,), torch.int32)
+            send_tok = self._buf("a2a_tok", (max(1, N * B),), torch.int32)
+            send_route = self._buf("a2a_route", (max(1, N * B), 2 * k), torch.int32)
+            pos = self._buf("a2a_pos", (N, max(1, B)), torch.int32)
+            send_x = self._buf("a2a_x", (max(1, N * B), H), x.dtype)
+            _lib.check(self.local.lib.glmx_ep_pack(sel.data_ptr(), w.data_ptr(), B, k, n, N, x.data_ptr(), H * x.element_size(),
+                                                   cnt.data_ptr(), cnt.data_ptr() + 4 * N, send_tok.data_ptr(),
+                                                   send_route.data_ptr(), pos.data_ptr(), send_x.data_ptr(), _stream_ptr(None)))
+            return cnt[:N], send_tok, send_route, pos, send_x
+        # the same order with tensor operations (CPU process groups: the host-logic tests)
+        owner = torch.where(sel >= 0, torch.div(sel, n, rounding_mode="floor"), torch.full_like(sel, -1))
+        mask = torch.zeros((N, B), dtype=torch.bool, device=x.device)
+        for j in range(k):
+            ok = (owner[:, j] >= 0) & (owner[:, j] < N)
+            mask[owner[ok, j].long(), torch.arange(B, device=x.device)[ok]] = True
+        d_idx, t_idx = mask.nonzero(as_tuple=True)
+        counts = mask.sum(dim=1).to(torch.int32)
+        pos = torch.full((N, B), -1, dtype=torch.int32, device=x.device)
+        pos[d_idx, t_idx] = torch.arange(d_idx.numel(), dtype=torch.int32, device=x.device)
+        s = sel[t_idx]
+        mine = owner[t_idx] == d_idx[:, None]
+        loc = torch.where(mine, s - d_idx[:, None].to(s.dtype) * n, torch.full_like(s, -1))
+        wl = torch.where(mine, w[t_idx], torch.zeros_like(w[t_idx]))
+        route = torch.cat([loc, wl.view(torch.int32)], dim=1).contiguous()
+        return counts, t_idx.to(torch.int32), route, pos, x[t_idx].contiguous()
+
+    def _forward_a2a(self, x, sel, w, mode, out):
+        B, H = x.shape
+        k = sel.shape[1]
+        N = self.world
+        cuda = self.device.type == "cuda"
+        self._mark(0)
+        if out is None:
+            out = torch.empty((B, H), dtype=torch.float32, device=self.device)
+        # the shared expert on the own rows does not wait for the exchange: a side stream runs it meanwhile
+        side_done = None
+        if self.has_shared:
+            ssel = self._buf(("sh_sel", B), (B, 1), torch.int32)
+            sw = self._buf(("sh_w", B), (B, 1), torch.float32)
+            ssel.fill_(self.n)
+            sw.fill_(1.0)
+            if cuda:
+                if self._side is None:
+                    self._side = torch.cuda.Stream(self.device)
+                    self._side_ws = None
+                ready = torch.cuda.Event()
+                ready.record(torch.cuda.current_stream(self.device))
+                self._side.wait_event(ready)
+                with torch.cuda.stream(self._side):
+                    need = self.local.workspace_bytes(B, 1)
+                    if self._side_ws is None or self._side_ws.numel() < need:
+                        self._side_ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
+                    self.local.forward(x, ssel, sw, mode=mode, out=out, workspace=self._side_ws)
+                    side_done = torch.cuda.Event()
+                    side_done.record(self._side)
+            else:
+                self.local.forward(x, ssel, sw, mode=mode, out=out)
+        else:
+            out.zero_()
+        counts, send_tok, send_route, pos, send_x = self._pack(x, sel, w)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        c = torch.stack([counts, recv_counts]).cpu()           # split sizes on the host (one synchronisation)
+        sc, rc = [int(v) for v in c[0]], [int(v) for v in c[1]]
+        S, R = sum(sc), sum(rc)
+        cap = max(1, N * B)                                    # a source sends each rank at most its B rows
+        recv_x = self._buf("a2a_rx", (cap, H), x.dtype)[:R]
+        recv_route = self._buf("a2a_rr", (cap, 2 * k), torch.int32)[:R]
+        dist.all_to_all_single(recv_x, send_x[:S], rc, sc, group=self.group)
+        dist.all_to_all_single(recv_route, send_route[:S], rc, sc, group=self.group)
+        self._mark(1)
+        # this shard's picks of the received rows
+        partial = self._buf("a2a_part", (cap, H), torch.float32)[:R]
+        if R:
+            self.local.forward(recv_x, recv_route[:, :k], recv_route[:, k:].view(torch.float32), mode=mode, out=partial)
+        self._mark(2)
+        # return: the results go back to the token owners in the order they were sent
+        ret = self._buf("a2a_ret", (cap, H), torch.float32)[:S]
+        dist.all_to_all_single(ret, partial, sc, rc, group=self.group)
+        if side_done is not None:
+            torch.cuda.current_stream(self.device).wait_event(side_done)
+        if cuda and hasattr(self.local, "lib"):
+            from . import _lib
+            from .layer import _stream_ptr
+            _lib.check(self.local.lib.glmx_ep_unpack_add(ret.data_ptr(), pos.data_ptr(), B, N, H, out.data_ptr(), _stream_ptr(None)))
+        else:
+            for d in range(N):
+                p = pos[d]
+                has = p >= 0
+                out[has] += ret[p[has].long()]
+        self._mark(3)
+        return out
+
+
+def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0, peer: bool = False,
+              exchange: str = "a2a") -> ExpertParallelLayer:
     """This rank's shard of a synth.ExpertBank (+ its shared expert), uploaded to `device`."""
     import numpy as np
 
@@ -264,4 +396,4 @@ def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0, peer: boo
     tr, ptrs, suh, svh = upload(experts)
     local = MoELayer(bank.H, bank.I, len(experts), ptrs, suh, svh, bits=bank.bits, has_shared=False, act_limit=act_limit,
                      keep=[tr], device=dev)
-    return ExpertParallelLayer(local, first, n, has_shared=bank.shared, group=group, E=bank.E, peer=peer)
+    return ExpertParallelLayer(local, first, n, has_shared=bank.shared, group=group, E=bank.E, peer=peer, exchange=exchange)

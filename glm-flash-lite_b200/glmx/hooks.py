@@ -16,8 +16,9 @@ import torch
 from .layer import MoELayer
 
 
-def attach(module, layer: MoELayer, mode: int = 2, max_bsz: int | None = None) -> None:
-    """Wrap module.routing_fn and module.cpu_split_combine to route every pick through `layer`."""
+def attach(module, layer: MoELayer, mode: int = 1, max_bsz: int | None = None) -> None:
+    """Wrap module.routing_fn and module.cpu_split_combine to route every pick through `layer`. mode 1 EXACT (default:
+    the exact-mode arithmetic of exllamav3's expert forward), 2 I16 (bit-identical to the reference's CPU I16 kernel)."""
     orig_route = module.routing_fn
     orig_comb = module.cpu_split_combine
     module._glmx_pending = None

@@ -142,12 +142,15 @@ class MoELayer:
                     pick_row=g(WS_PICK_ROW, torch.int32, ntok * topk),
                     jobs=g(WS_JOBS, torch.int32, 4 * J).reshape(J, 4))
 
-    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = _lib.MODE_I16,
+    def forward(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: int = _lib.MODE_EXACT,
                 out: torch.Tensor | None = None, out_dtype=torch.float32, accumulate: bool = False,
-                stream=None, events=None) -> torch.Tensor:
+                stream=None, events=None, workspace: torch.Tensor | None = None) -> torch.Tensor:
         """out [ntok, H] = sum over each token's picks of w * expert(x) (+ shared expert).
-        mode: 2 I16 (default; bit-identical to the reference's I16 kernel), 1 EXACT (fp16 weights, fp32 accumulation).
-        events: optional list of _lib.PHASES torch.cuda.Event recorded between the kernels on the launching stream."""
+        mode: 1 EXACT (default: fp16 codebook weights, fp32 accumulation, the reference's EXACT arithmetic), 2 I16
+        (bit-identical to the reference's I16 kernel; int16 activations, outside the 2e-3 bar at H=6144).
+        events: optional list of _lib.PHASES torch.cuda.Event recorded between the kernels on the launching stream.
+        workspace: a uint8 CUDA tensor of at least workspace_bytes(ntok, topk) to use instead of the layer's own (calls
+        that may run at the same time on different streams need workspaces of their own)."""
         x = x.contiguous(); sel = sel.contiguous(); w = w.contiguous()
         ntok = x.shape[0]
         topk = sel.shape[1] if sel.dim() == 2 else 0
@@ -158,7 +161,12 @@ class MoELayer:
                 raise ValueError(f"tensor on {t.device}, layer on {self.device}")
         if out is None:
             out = torch.empty((ntok, self.H), dtype=out_dtype, device=self.device)
-        ws = self.workspace(ntok, topk)
+        if workspace is not None:
+            if workspace.numel() < self.workspace_bytes(ntok, topk) or workspace.device != self.device:
+                raise ValueError("workspace too small or on another device")
+            ws = workspace
+        else:
+            ws = self.workspace(ntok, topk)
         ev = None
         if events is not None:
             for e in events:

@@ -8,8 +8,10 @@ live in HBM instead of a pinned host arena served by a CPU worker:
   accepted and ignored (there is no worker, no handshake and no block-contiguous CPU copy).
 * tier_add_layer's `ptrs` [E, 3] are device addresses of the native-layout gate / up / down trellis tensors (the
   HBM-resident copies exllamav3 already holds, glm53/expert_cache.py:603-616), not host addresses.
-* tier_forward runs on the GPU. Mode -1 (auto) selects I16, which here is valid for any tokens-per-expert (the
-  reference selects it for <= 2, ft_tier_ext.cpp:899-900); mode 0 (AFFINE) has no GPU kernel and is rejected.
+* tier_forward runs on the GPU. Mode -1 (auto) follows the reference's rule (ft_tier_ext.cpp:899-900): I16 when no
+  expert has more than 2 of the call's tokens, where the reference's I16 is valid (H <= 4096, its scratch limit,
+  ft_core.h:1353); otherwise EXACT, in place of the reference's AFFINE, which is a CPU shortcut with no GPU kernel here.
+  Mode 0 (AFFINE) is rejected.
   The result is returned on x's device (a CPU x gets a CPU result, as in the reference).
 """
 from __future__ import annotations
@@ -20,7 +22,14 @@ import torch
 
 from .layer import MoELayer
 
-_MODES = {-1: 2, 1: 1, 2: 2}
+_MODES = {-1: None, 1: 1, 2: 2}
+
+
+def _auto_mode(sel: torch.Tensor, H: int) -> int:
+    """tier_forward's mode -1: I16 for <= 2 tokens per expert at H <= 4096 (the reference's rule and range), else EXACT."""
+    s = sel[sel >= 0]
+    most = int(torch.bincount(s.reshape(-1).long()).max()) if s.numel() else 0
+    return 2 if most <= 2 and H <= 4096 else 1
 
 
 class _Tier:
@@ -96,8 +105,8 @@ def tier_forward(li, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, mode: 
     _check(x.dim() == 2 and x.shape[1] == T.H, "tier_forward: x must be [m, H]")
     dev = layer.device
     t0 = time.perf_counter_ns()
-    out = layer.forward(x.to(dev, non_blocking=True), sel.to(dev, torch.int32), w.to(dev, torch.float32),
-                        mode=_MODES[int(mode)])
+    m = _MODES[int(mode)] if int(mode) != -1 else _auto_mode(sel, T.H)
+    out = layer.forward(x.to(dev, non_blocking=True), sel.to(dev, torch.int32), w.to(dev, torch.float32), mode=m)
     res = out.to(x.device)
     T.stats["busy_ns"] += time.perf_counter_ns() - t0
     T.stats["jobs"] += 1

@@ -184,6 +184,19 @@ GLMX_API int glmx_peer_reduce(const float* recv, const int* flags, int world, in
  * [own_begin, own_end) (the rank's own rows) and -1 elsewhere. */
 GLMX_API int glmx_ep_split(const int* route, int rows, int topk, int first, int n, int shared, int own_begin, int own_end,
                            int* loc, float* w, void* stream);
+/* No counterpart (expert parallelism). The all-to-all form of the dispatch and return (glmx.ep, exchange "a2a"): every
+ * rank sends each token row only to the ranks that own at least one of its picks, and gets back only those rows' partial
+ * results. glmx_ep_pack, on the token owner: sel int32 / w fp32 [B][topk] (global ids; rank d owns ids
+ * [d * experts_per_rank, (d + 1) * experts_per_rank), others and negative ids are skipped) and x [B] rows of row_bytes
+ * bytes -> counts int32 [world] (rows for each rank), *total (their sum), send_tok int32 [B * world] (each send row's
+ * token), send_route int32 [B * world][2 * topk] (the row's picks in the destination's local ids, -1 with weight 0
+ * elsewhere, then the weights' fp32 bits), pos int32 [world][B] (send row of (rank, token) or -1) and send_x
+ * [B * world] rows (x gathered), all in (destination, token) order. glmx_ep_unpack_add, after the return: out fp32
+ * [B][hidden] += the returned rows ret fp32 [*total][hidden] (in send order) of each token, added in rank order. */
+GLMX_API int glmx_ep_pack(const int* sel, const float* w, int B, int topk, int experts_per_rank, int world, const void* x,
+                          int row_bytes, int* counts, int* total, int* send_tok, int* send_route, int* pos, void* send_x,
+                          void* stream);
+GLMX_API int glmx_ep_unpack_add(const float* ret, const int* pos, int B, int world, int hidden, float* out, void* stream);
 /* No counterpart (expert parallelism). CUDA IPC for those buffers: glmx_ipc_alloc makes a zeroed device allocation of its own (the mapping in another
  * process then starts at the buffer), glmx_ipc_handle its handle (GLMX_IPC_HANDLE_BYTES bytes), glmx_ipc_open maps a
  * peer's handle, glmx_ipc_close / glmx_ipc_free undo them. */

@@ -313,12 +313,13 @@ def with_shared_routes(sel: np.ndarray, w: np.ndarray, E: int):
 
 # EXACT-mode parity rule (one rule for the tests and the smoke check). The north-star bar is max-abs <= 2e-3 x RMS of
 # the output; at H=6144 the reference's own fp32 kernels sit above it (its fp16 rounding points turn accumulation-order
-# differences into 1-ulp flips), so the bar is the larger of 2e-3 and EXACT_SLACK x the distance of the reference's more
-# accurate schedule (moe_forward_band, ft_core.h:1617-1651) from the fp64 restatement on the same inputs; rel-RMS must
-# be within EXACT_SLACK of the reference's own EXACT kernels' (the larger of moe_forward and moe_forward_band), with a
-# floor of EXACT_RELRMS_FLOOR for inputs where both happen to be almost exact. The slack covers single 1-ulp flips at
-# an fp16 rounding point, which dominate both metrics on any one input; averaged over many inputs the tests require
-# the GPU to be at least as close to the fp64 restatement as the band kernel.
+# differences into 1-ulp flips). On one input the bars are: max-abs within the larger of 2e-3 and EXACT_SLACK x the
+# distance of the reference's own EXACT kernels (moe_forward and its band schedule, ft_core.h:1338-1407, 1617-1651)
+# from the fp64 restatement, rel-RMS within EXACT_SLACK x theirs, with a floor of EXACT_RELRMS_FLOOR for inputs where
+# both happen to be almost exact. A single 1-ulp flip at an fp16 rounding point, which any fp32 accumulation order makes
+# on some inputs, dominates both metrics on that input, so the per-input bars accept what the reference's own kernels
+# show; averaged over many inputs the tests require the GPU to be at least as close to the fp64 restatement as the band
+# kernel, the more accurate of the two.
 EXACT_MAXABS = 2e-3
 EXACT_SLACK = 1.25
 EXACT_RELRMS_FLOOR = 5e-5
@@ -327,17 +328,11 @@ EXACT_RELRMS_FLOOR = 5e-5
 def exact_bars(oracle_fp64: np.ndarray, ref_fp32: np.ndarray | None = None, band_fp32: np.ndarray | None = None):
     """(max-abs bar, rel-RMS bar) of the EXACT-mode rule for one input, from the reference's own outputs on it
     (either may be None: the bar then rests on the other, or on the north-star values when both are absent)."""
-    bar_mx, bar_rr = EXACT_MAXABS, EXACT_RELRMS_FLOOR
-    refs = [r for r in (ref_fp32, band_fp32) if r is not None]
-    if band_fp32 is not None:
-        bar_mx = max(bar_mx, EXACT_SLACK * rel_err(band_fp32, oracle_fp64)[0])
-    elif ref_fp32 is not None:
-        bar_mx = max(bar_mx, EXACT_SLACK * rel_err(ref_fp32, oracle_fp64)[0])
-    if refs:
-        bar_rr = max([bar_rr] + [EXACT_SLACK * rel_err(r, oracle_fp64)[1] for r in refs])
-    else:
-        bar_rr = 5e-4
-    return bar_mx, bar_rr
+    refs = [rel_err(r, oracle_fp64) for r in (ref_fp32, band_fp32) if r is not None]
+    if not refs:
+        return EXACT_MAXABS, 5e-4
+    return (max([EXACT_MAXABS] + [EXACT_SLACK * m for m, _ in refs]),
+            max([EXACT_RELRMS_FLOOR] + [EXACT_SLACK * r for _, r in refs]))
 
 
 def rel_err(a: np.ndarray, ref: np.ndarray):

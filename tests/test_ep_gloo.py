@@ -58,12 +58,12 @@ def reference(x, sel, w):
     return out
 
 
-def _worker(rank, world, port, B, q):
+def _worker(rank, world, port, B, q, exchange):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         first, n = ep.shard_range(E, world, rank)
-        layer = ep.ExpertParallelLayer(FakeShard(first, n), first, n, has_shared=True, E=E)
+        layer = ep.ExpertParallelLayer(FakeShard(first, n), first, n, has_shared=True, E=E, exchange=exchange)
         x, sel, w = inputs(rank, B)
         out = layer.forward(x, sel, w)
         err = float((out - reference(x, sel, w)).abs().max())
@@ -78,12 +78,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2])
-def test_ep_two_ranks_match_single_process(world):
+@pytest.mark.parametrize("world,exchange", [(2, "a2a"), (2, "allgather"), (4, "a2a")])
+def test_ep_ranks_match_single_process(world, exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 5, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 5, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)

@@ -34,14 +34,16 @@ def test_tier_forward_matches_oracle(oracle):
         sel[1, 2] = -1
         xt, st, wt = torch.from_numpy(x.astype(np.float32)), torch.from_numpy(sel), torch.from_numpy(w)
         want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=2)
-        for mode in (-1, 2):
-            got = tier.tier_forward(0, xt, st, wt, mode)
-            assert got.device.type == "cpu" and got.dtype == torch.float32
-            np.testing.assert_array_equal(got.numpy(), want)
+        got = tier.tier_forward(0, xt, st, wt, 2)
+        assert got.device.type == "cpu" and got.dtype == torch.float32
+        np.testing.assert_array_equal(got.numpy(), want)
+        # auto (-1): the reference's rule picks I16 or EXACT; the result is that mode's, bit for bit
+        auto = tier.tier_forward(0, xt, st, wt, -1)
+        np.testing.assert_array_equal(auto.numpy(), tier.tier_forward(0, xt, st, wt, tier._auto_mode(st, H)).numpy())
         got = tier.tier_forward(0, xt, st, wt, 1).numpy()
         assert_exact_mode(got, oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1),
                           *reference_outputs(bank, x, sel, w), label="tier EXACT")
-        assert tier.tier_stats()[0] == 3
+        assert tier.tier_stats()[0] == 5
     finally:
         tier.tier_reset()
     del tr
