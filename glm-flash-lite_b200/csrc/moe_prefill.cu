@@ -573,9 +573,12 @@ cudaError_t launch_prefill_forward(const Layer& L, const void* x, int x_dtype, i
         g.trellis = L.d_trellis;
         g.err = reinterpret_cast<int*>(ws + lay.err);
         g.proj0 = 0; g.nproj = 2; g.nslot = 2; g.slot0 = 0; g.kt = L.H / 16; g.ntn = L.I / 16; g.ndim = L.I;
-        // split K so that every split holds a whole number of 128-input blocks per accumulator chain
-        const int nblk = L.H / 128;
-        g.ksplit = nblk % (PF_KSPLIT * 4) == 0 ? PF_KSPLIT : 1;
+        // split K (at most PF_KSPLIT ways) so that every split holds a whole number of 128-input blocks per accumulator
+        // chain (2 chains at TN = 256, 4 at TN = 128): the most splits that divide, the shortest tensor-core chains
+        const int nblk = L.H / 128, nch = pf_tile_n(L.I) == 256 ? 2 : 4;
+        g.ksplit = 1;
+        for (int ks = PF_KSPLIT; ks > 1; --ks)
+            if (nblk % (ks * nch) == 0) { g.ksplit = ks; break; }
         g.split_stride = (size_t) rows * 2 * L.I;
         g.yraw = reinterpret_cast<float*>(ws + lay.yraw_gu);
         if (L.bits[0] == L.bits[1])

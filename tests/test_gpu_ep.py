@@ -1,6 +1,6 @@
 """Expert parallelism on 2 GPUs (NCCL): each rank's output against the single-GPU layer over the same global batch, with
-the return over peer memory (combine writing into the owner's buffer) and with NCCL's reduce-scatter. Skipped on a box
-with fewer than 2 GPUs."""
+each exchange: per-destination all-to-all (a2a), all-gather + the return over peer memory (combine writing into the
+owner's buffer), all-gather + NCCL's reduce-scatter. Skipped on a box with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -45,10 +45,11 @@ def _worker(rank, world, port, q):
         xs = [_inputs(r) for r in range(world)]
         xg = np.concatenate([a for a, _, _ in xs]); sg = np.concatenate([s for _, s, _ in xs]); wg = np.concatenate([w for _, _, w in xs])
         res = {}
-        for peer in (True, False):
-            layer = ep.from_bank(bank, device=dev, peer=peer)
+        for exch in ("peer", "allgather", "a2a"):
+            peer = exch == "peer"
+            layer = ep.from_bank(bank, device=dev, peer=peer, exchange="allgather" if peer else exch)
             layers.append(layer)
-            assert layer.peer == peer
+            assert layer.exchange == exch
             for mode in (2, 1):
                 x, s, w = (torch.from_numpy(a).to(dev) for a in xs[rank])
                 got = layer.forward(x, s, w, mode=mode)
@@ -59,7 +60,7 @@ def _worker(rank, world, port, q):
                 g, wnt = got.cpu().numpy().astype(np.float64), want.cpu().numpy().astype(np.float64)
                 rms = float(np.sqrt(np.mean(wnt * wnt)))
                 same = bool(np.array_equal(got.cpu().numpy(), got2.cpu().numpy()) and np.array_equal(got.cpu().numpy(), got3.cpu().numpy()))
-                res[(peer, mode)] = (float(np.max(np.abs(g - wnt))) / rms, same, got.cpu().numpy())
+                res[(exch, mode)] = (float(np.max(np.abs(g - wnt))) / rms, same, got.cpu().numpy())
             if peer:
                 res["peer_err"] = layer._ret.error_flags()
         q.put((rank, res))
@@ -94,12 +95,12 @@ def test_ep_two_gpus_match_single_gpu(oracle):
     for r, v in res.items():
         assert isinstance(v, dict), (r, v)
         assert v["peer_err"] == 0, (r, v)
-        for peer in (True, False):
+        for exch in ("peer", "allgather", "a2a"):
             # I16: per-expert results are bit-identical; only the order of the cross-shard sum differs
-            assert v[(peer, 2)][0] <= 1e-5 and v[(peer, 2)][1], (r, peer, v[(peer, 2)][:2])
+            assert v[(exch, 2)][0] <= 1e-5 and v[(exch, 2)][1], (r, exch, v[(exch, 2)][:2])
             # EXACT: the shard's split-K schedule differs from the full layer's (fp16 rounding points may flip), so
             # the output is held to the EXACT-mode bar against the fp64 restatement, like every EXACT output
-            assert v[(peer, 1)][1], (r, peer)
+            assert v[(exch, 1)][1], (r, exch)
             rows = slice(r * B, (r + 1) * B)
-            assert_exact_mode(v[(peer, 1)][2], exact[rows], None if ref_out is None else ref_out[rows],
-                              None if band_out is None else band_out[rows], label=f"ep rank {r} peer {peer}")
+            assert_exact_mode(v[(exch, 1)][2], exact[rows], None if ref_out is None else ref_out[rows],
+                              None if band_out is None else band_out[rows], label=f"ep rank {r} {exch}")
