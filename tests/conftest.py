@@ -81,6 +81,17 @@ def assert_exact_mode(gpu, oracle_fp64, ref_fp32=None, band_fp32=None, label="",
     return g_mx, g_rr
 
 
+def oracle_threads(oracle, bank, x, sel, w, mode=1, threads=8):
+    """oracle.moe_forward over token chunks on host threads (the C restatement runs outside the GIL; tokens are
+    independent given their picks), for samples of dozens of tokens at H=6144."""
+    from concurrent.futures import ThreadPoolExecutor
+    x = np.ascontiguousarray(x, np.float32); sel = np.ascontiguousarray(sel); w = np.ascontiguousarray(w)
+    chunks = [c for c in np.array_split(np.arange(x.shape[0]), threads) if c.size]
+    with ThreadPoolExecutor(len(chunks)) as ex:
+        parts = list(ex.map(lambda c: oracle.moe_forward(bank, x[c], sel[c], w[c], mode=mode), chunks))
+    return np.concatenate(parts)
+
+
 def reference_outputs(bank, x, sel, w, threads=8):
     """The reference's own EXACT kernels on one input: (moe_forward, moe_forward_band) outputs, or (None, None) where
     oracle/_ref was not built. The shared expert is folded in as a weight-1 pick."""

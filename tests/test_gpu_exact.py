@@ -9,7 +9,7 @@ fp64 restatement as the band kernel (the more accurate of the two), in both metr
 import numpy as np
 import pytest
 
-from conftest import assert_exact_mode, parity, reference_outputs
+from conftest import assert_exact_mode, oracle_threads, parity, reference_outputs
 
 pytestmark = pytest.mark.gpu
 
@@ -117,7 +117,7 @@ def test_bench_config_parity(oracle, dev, big_layer, mode):
     bank = _host_bank(big_layer, touched)
     ss = np.vectorize(remap.get)(sel[rows]).astype(np.int32)
     xs, ws = x[rows].astype(np.float32), w[rows]
-    want = oracle.moe_forward(bank, xs, ss, ws, mode=mode)
+    want = oracle_threads(oracle, bank, xs, ss, ws, mode=mode)
     if mode == 2:
         np.testing.assert_array_equal(got[rows], want)
     else:
@@ -148,3 +148,28 @@ def test_exact_vs_i16_consistent(dev, big_layer):
     b = layer.forward(t(x), t(sel), t(w), mode=2).cpu().numpy()
     mx, rr = parity(b, a)
     assert rr < 2e-3 and mx < 1.5e-2, (mx, rr)
+
+
+def test_prefill_config_parity(oracle, dev, big_layer):
+    """configs[2] on the same layer: 4096 tokens of bf16 activations, expert popularity Zipf(1.1), top-8, EXACT on the
+    tensor-core GEMM path; 64 seeded tokens checked against the fp64 restatement and the reference's own kernels
+    (moe_forward and moe_forward_band) on the same inputs."""
+    from glmx import _lib, synth
+    layer = big_layer[0]
+    T = 4096
+    sel, w = synth.route_zipf(T, E6, 8, 1.1, 7101)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7102)
+    xb = torch.randn((T, H6), device=dev, generator=g).to(torch.bfloat16)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    got = layer.forward(xb, t(sel), t(w), mode=_lib.MODE_EXACT | _lib.PATH_GEMM).cpu().numpy()
+    assert layer.check_device(T, 8) == 0 and np.isfinite(got).all()
+    rows = np.sort(np.random.default_rng(7103).choice(T, 64, replace=False))
+    touched = np.unique(sel[rows])
+    remap = {int(e): i for i, e in enumerate(touched)}
+    bank = _host_bank(big_layer, touched)
+    ss = np.vectorize(remap.get)(sel[rows]).astype(np.int32)
+    # the layer's input domain: bf16 values rounded to fp16 at ingress
+    xs = xb[torch.from_numpy(rows).to(dev)].float().half().float().cpu().numpy()
+    want = oracle_threads(oracle, bank, xs, ss, w[rows], mode=1)
+    assert_exact_mode(got[rows], want, *reference_outputs(bank, xs, ss, w[rows]), label="configs[2] T=4096 Zipf(1.1) E=288")

@@ -73,3 +73,20 @@ def test_hooks_with_gpu_layer(oracle):
     out = m.cpu_split_combine(fhs, None, None, None).cpu()
     want = oracle.moe_forward(bank, x.astype(np.float32), sel, w.astype(np.float16).astype(np.float32), mode=2)
     np.testing.assert_array_equal(out.numpy(), want.astype(np.float16))
+
+
+def test_layer_from_exllamav3_matches_bank():
+    """The on-disk EXL3 adapter (per-expert trellis tensors, as exllamav3 holds them) gives the same layer as the
+    packed bank: bit-identical outputs in both modes."""
+    from glmx import MoELayer, hooks, synth
+    from test_host_api import fake_exl3_module
+    dev = torch.device("cuda", 0)
+    bank = synth.make_bank(1024, 512, 6, shared=False, seed=71)
+    m = fake_exl3_module(bank, device=dev)
+    a = hooks.layer_from_exllamav3(m)
+    b = MoELayer.from_bank(bank, device=dev)
+    x = torch.from_numpy(synth.make_x(5, 1024, 72)).to(dev)
+    s, w = synth.route_uniform(5, 6, 3, 73)
+    s, w = torch.from_numpy(s).to(dev), torch.from_numpy(w).to(dev)
+    for mode in (1, 2):
+        assert torch.equal(a.forward(x, s, w, mode=mode), b.forward(x, s, w, mode=mode)), mode

@@ -134,3 +134,62 @@ def test_hooks_bypass():
         assert torch.equal(wo, w) and not layer.calls
         fhs = torch.ones(bsz, 256)
         assert torch.equal(mod.cpu_split_combine(fhs, None, None, None), fhs)
+
+
+# ---- on-disk EXL3 adapter: hooks.layer_from_exllamav3 over exllamav3's per-expert tensors ----------------------------
+
+class _Inner:
+    def __init__(self, trellis, suh, svh):
+        self.trellis, self.suh, self.svh = trellis, suh, svh
+
+
+class _Linear:
+    def __init__(self, inner):
+        self.inner = inner
+
+
+class _Multi:
+    def __init__(self, linears):
+        self.linears = linears
+
+
+def fake_exl3_module(bank, device="cpu", act_limit=0.0):
+    """A stand-in for exllamav3's BlockSparseMLP with the attributes the reference's cpu_tier reads
+    (multi_{gate,up,down}.linears[e].inner.{trellis, suh, svh}, hidden/intermediate sizes, act_limit; glm53/cpu_tier.py:
+    535-537, glm53/expert_cache.py:603-616): one trellis tensor per expert and projection (its own allocation, as
+    exllamav3 loads them), suh/svh fp16 vectors."""
+    import numpy as np
+
+    class M:
+        pass
+    m = M()
+    m.hidden_size, m.intermediate_size, m.act_limit = bank.H, bank.I, act_limit
+    for p, name in enumerate(("multi_gate", "multi_up", "multi_down")):
+        lins = []
+        for e in range(bank.E):
+            tr = torch.from_numpy(np.ascontiguousarray(bank.proj(e, p)).view(np.int16).copy()).to(device)
+            lins.append(_Linear(_Inner(tr, torch.from_numpy(bank.suh[p][e].copy()).to(device),
+                                       torch.from_numpy(bank.svh[p][e].copy()).to(device))))
+        setattr(m, name, _Multi(lins))
+    return m
+
+
+def test_layer_from_exllamav3_tables(monkeypatch):
+    """The adapter's pointer table, scales and sizes (host logic; the layer class is recorded, not built)."""
+    from glmx import hooks, synth
+    bank = synth.make_bank(256, 128, 5, shared=False, seed=3)
+    m = fake_exl3_module(bank, act_limit=10.0)
+    seen = {}
+
+    class Rec:
+        def __init__(self, H, I, E, ptrs, suh, svh, **kw):
+            seen.update(H=H, I=I, E=E, ptrs=ptrs, suh=suh, svh=svh, **kw)
+    monkeypatch.setattr(hooks, "MoELayer", Rec)
+    hooks.layer_from_exllamav3(m, device="cpu")
+    assert (seen["H"], seen["I"], seen["E"]) == (256, 128, 5) and seen["act_limit"] == 10.0 and not seen["has_shared"]
+    for e in range(5):
+        for p, name in enumerate(("multi_gate", "multi_up", "multi_down")):
+            inner = getattr(m, name).linears[e].inner
+            assert int(seen["ptrs"][e, p]) == inner.trellis.data_ptr()
+            assert torch.equal(seen["suh"][p][e], inner.suh) and torch.equal(seen["svh"][p][e], inner.svh)
+    assert len(seen["keep"]) == 15
