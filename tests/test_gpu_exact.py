@@ -2,10 +2,11 @@
 benchmarked configuration itself (configs[1]: B=64 over 288 routed experts + shared, both modes), and run-to-run
 determinism of the decode kernels (work taken from counters, split-K finished by whichever CTA arrives last).
 
-The EXACT rule (oracle.exact_bars, the same as the smoke check), on each input: max-abs within max(2e-3, 1.25 x the
-distance of the reference's own EXACT kernels - moe_forward and its band schedule moe_forward_band - from the fp64
-restatement) and rel-RMS within 1.25 x theirs; over all seeded inputs together the GPU must be at least as close to the
-fp64 restatement as the band kernel (the more accurate of the two), in both metrics."""
+The EXACT rule (oracle.exact_bars, the same as the smoke check), on each input: max-abs within the largest of 2e-3,
+1.25 x the distance of the reference's own EXACT kernels - moe_forward and its band schedule moe_forward_band - from the
+fp64 restatement, and one fp16 step at the largest output (a single rounding flip there); rel-RMS within 1.25 x the
+reference kernels'; over all seeded decode inputs together the GPU must be at least as close to the fp64 restatement
+as the band kernel (the more accurate of the two), in both metrics."""
 import numpy as np
 import pytest
 
