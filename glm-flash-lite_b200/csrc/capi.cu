@@ -232,6 +232,9 @@ static int forward_impl(const glmx_layer* l, const void* x, int x_dtype, int nto
         e = launch_prefill_forward(l->L, x, x_dtype, ntok, topk, out, out_dtype, accumulate, wsb, lay, st, events, hc);
     else
         e = launch_decode_forward(l->L, x, x_dtype, ntok, topk, base, out, out_dtype, accumulate, wsb, lay, grid, st, events, hc);
+    // the next site's mix partials: fused into the EXACT GEMV path's combine, a pass over the updated stack otherwise
+    if (e == cudaSuccess && hc && hc->fn && (base == GLMX_MODE_I16 || gemm))
+        e = launch_hc_apply_partials(hc->x, nullptr, 0, nullptr, nullptr, hc->fn, hc->part, ntok, l->L.H, 0, st);
     if (e != cudaSuccess) return cuda_fail(e, "glmx_moe_forward: launch");
     return GLMX_OK;
 }
@@ -255,6 +258,55 @@ int glmx_moe_forward_hc(const glmx_layer* l, const void* x, int x_dtype, int nto
     const HcOut hc{ hc_x, hc_post, hc_comb, y_dtype == GLMX_F16 ? 1 : 0 };
     return forward_impl(l, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, nullptr, GLMX_F32, 0, ws, ws_bytes, stream,
                         nullptr, &hc);
+}
+
+int glmx_moe_forward_hc_mix(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,
+                            const void* w, int w_dtype, int topk, int mode, float* hc_x, const float* hc_post,
+                            const float* hc_comb, int y_dtype, const uint16_t* fn, float* partials, void* ws, size_t ws_bytes,
+                            void* stream)
+{
+    if (ntok > 0 && (!hc_x || !hc_post || !hc_comb || !fn || !partials))
+        return fail(GLMX_E_ARG, "glmx_moe_forward_hc_mix: null stream stack / post / comb / fn / partials");
+    if (y_dtype != GLMX_F16 && y_dtype != GLMX_F32) return fail(GLMX_E_ARG, "glmx_moe_forward_hc_mix: y dtype must be fp16 or fp32");
+    if (!aligned16(hc_x) || !aligned16(fn)) return fail(GLMX_E_ARG, "glmx_moe_forward_hc_mix: x and fn must be 16-byte aligned");
+    HcOut hc{ hc_x, hc_post, hc_comb, y_dtype == GLMX_F16 ? 1 : 0 };
+    hc.fn = reinterpret_cast<const __half*>(fn);
+    hc.part = partials;
+    return forward_impl(l, x, x_dtype, ntok, sel, sel_dtype, w, w_dtype, topk, mode, nullptr, GLMX_F32, 0, ws, ws_bytes, stream,
+                        nullptr, &hc);
+}
+
+int glmx_hc_apply_partials(float* x, const void* y, int y_dtype, const float* post, const float* comb, const uint16_t* fn,
+                           float* partials, int R, int D, void* stream)
+{
+    if (R < 0 || D <= 0 || D % 128) return fail(GLMX_E_ARG, "glmx_hc_apply_partials: R >= 0 rows, D a multiple of 128");
+    if (R == 0) return GLMX_OK;
+    if (!x || !fn || !partials) return fail(GLMX_E_ARG, "glmx_hc_apply_partials: null x / fn / partials");
+    if (y && (!post || !comb || (y_dtype != GLMX_F16 && y_dtype != GLMX_F32)))
+        return fail(GLMX_E_ARG, "glmx_hc_apply_partials: y needs post, comb and an fp16 or fp32 dtype");
+    if (!aligned16(x) || !aligned16(fn) || (y && !aligned16(y)))
+        return fail(GLMX_E_ARG, "glmx_hc_apply_partials: x, y and fn must be 16-byte aligned");
+    const cudaError_t e = launch_hc_apply_partials(x, y, y_dtype == GLMX_F16, post, comb, reinterpret_cast<const __half*>(fn),
+                                                   partials, R, D, y ? 1 : 0, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? GLMX_OK : cuda_fail(e, "glmx_hc_apply_partials: launch");
+}
+
+int glmx_hc_finalize_norm(const float* x, const float* partials, int R, int D, const float* base, const float* scale,
+                          float* post, float* comb, const void* nw, int nw_dtype, uint16_t* out, float rms_eps, float hc_eps,
+                          int iters, float n_eps, float cbias, float cscale, void* stream)
+{
+    if (R < 0 || D <= 0 || D % 512 || D > 16384)
+        return fail(GLMX_E_ARG, "glmx_hc_finalize_norm: D a multiple of 512 up to 16384 (8 warps of partial chunks)");
+    if (R == 0) return GLMX_OK;
+    if (!x || !partials || !base || !scale || !post || !comb || !nw || !out)
+        return fail(GLMX_E_ARG, "glmx_hc_finalize_norm: null argument");
+    if (nw_dtype != GLMX_F16 && nw_dtype != GLMX_BF16) return fail(GLMX_E_ARG, "glmx_hc_finalize_norm: norm weight fp16 or bf16");
+    if (iters < 1) return fail(GLMX_E_ARG, "glmx_hc_finalize_norm: iters >= 1");
+    if (!aligned16(x) || !aligned16(out)) return fail(GLMX_E_ARG, "glmx_hc_finalize_norm: x and out must be 16-byte aligned");
+    const cudaError_t e = launch_hc_finalize(x, partials, base, scale, post, comb, nw, nw_dtype == GLMX_BF16,
+                                             reinterpret_cast<__half*>(out), R, D, rms_eps, hc_eps, iters, n_eps, cbias,
+                                             cscale, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? GLMX_OK : cuda_fail(e, "glmx_hc_finalize_norm: launch");
 }
 
 int glmx_moe_forward_peer(const glmx_layer* l, const void* x, int x_dtype, int ntok, const void* sel, int sel_dtype,

@@ -318,6 +318,36 @@ __device__ __forceinline__ void hc_apply_col(float* x_row, int D, int c, float y
     }
 }
 
+// hc_mix_partials of one (row, stream, 128-column block) on a warp whose lane l holds the updated column quad
+// jb * 32 + l of that stream (glm53/k_hcfuse.py:92-126): per lane the sum of squares (fma chain from 0) and s . fn_j for
+// the 24 mix rows (fma chain from s.w * w.w, added to 0), then the warp's shfl_down tree; lane 0 stores the 25 sums at
+// part[0..24]. fn_q points at the quad's 4 weights of mix row 0, rows fn_row elements apart. All 32 lanes must be active.
+__device__ __forceinline__ void hc_mix_warp(float4 s, const __half* fn_q, size_t fn_row, float* part, int lane)
+{
+    float acc[25];
+    acc[24] = 0.0f;
+    acc[24] = fmaf(s.x, s.x, acc[24]);
+    acc[24] = fmaf(s.y, s.y, acc[24]);
+    acc[24] = fmaf(s.z, s.z, acc[24]);
+    acc[24] = fmaf(s.w, s.w, acc[24]);
+#pragma unroll
+    for (int j = 0; j < 24; ++j)
+    {
+        const uint2 pk = *reinterpret_cast<const uint2*>(fn_q + (size_t) j * fn_row);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&pk.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&pk.y));
+        acc[j] = 0.0f + fmaf(s.x, lo.x, fmaf(s.y, lo.y, fmaf(s.z, hi.x, __fmul_rn(s.w, hi.y))));
+    }
+#pragma unroll
+    for (int k = 0; k < 25; ++k)
+    {
+        float v = acc[k];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
+        if (lane == 0) part[k] = v;
+    }
+}
+
 // ---- 128-point transforms on one warp (lane holds v[q] = element lane + 32 q) ------------------------------------------
 
 // Unnormalised Walsh-Hadamard butterfly in the reference's stage order w = 1, 2, ..., 64 (ft_core.h:89-94):

@@ -1,6 +1,7 @@
 // Internal (non-ABI) declarations shared by the .cu files of libglmx.
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -81,6 +82,8 @@ struct HcOut
     const float* comb;     // [ntok][4][4], comb[h][g]
     int y_half;            // 1: y is rounded to fp16 first (an fp16 sublayer output), 0: fp32
     PeerOut peer;          // peer.recv != nullptr (and x == nullptr): expert-parallel return instead of out
+    const __half* fn;      // != nullptr: also the next site's hc_mix_partials of the updated stack: fn [24][4H] fp16
+    float* part;           // [ntok][4H/128][25] fp32 mix partial sums
 };
 
 // A kernel launch that may overlap the previous kernel of the stream (programmatic dependent launch); the kernel must
@@ -123,9 +126,20 @@ cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, int nt
 cudaError_t launch_combine_raw(const Layer& L, const float* yraw, int ntok, int topk, void* out, int out_dtype, int accumulate,
                                uint8_t* ws, const WsLayout& lay, cudaStream_t st, const HcOut* hc = nullptr);
 
+// hyper-connection site kernels (hc.cu): hc_apply (apply != 0) + hc_mix_partials (part != nullptr) over R rows of
+// [4][D] stream stacks; hc_mix_finalize + RMSNorm
+cudaError_t launch_hc_apply_partials(float* x, const void* y, int y_half, const float* post, const float* comb,
+                                     const __half* fn, float* part, int R, int D, int apply, cudaStream_t st);
+cudaError_t launch_hc_finalize(const float* x, const float* part, const float* base, const float* scale, float* post,
+                               float* comb, const void* nw, int nw_bf16, __half* out, int R, int D, float rms_eps,
+                               float hc_eps, int iters, float n_eps, float cbias, float cscale, cudaStream_t st);
+
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
+#ifndef GLMX_EXACT_TC
+#define GLMX_EXACT_TC 0            // 1: EXACT GEMV dot products as tensor-core MMAs from zero per 16-input tile
+#endif
 #ifndef GLMX_EXACT_MAXM
-#define GLMX_EXACT_MAXM 4
+#define GLMX_EXACT_MAXM (GLMX_EXACT_TC ? 8 : 4)
 #endif
 constexpr int EXACT_MAXM = GLMX_EXACT_MAXM;   // rows per job of the EXACT decode GEMV (per-row accumulators in registers)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)

@@ -30,6 +30,9 @@ constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
 constexpr int XROW = 256;    // bytes per staged activation row: one 128-input block, fp16, in the lane order of gemv_xpos
+// stride of the staged activation rows in a stage: the tensor-core form reads row g at lane (g, tq), and a 320-byte
+// stride puts the two rows of each quarter-warp's 16-byte loads in different bank halves
+constexpr int XSTR = GLMX_EXACT_TC ? 320 : XROW;
 #ifndef GLMX_EXACT_CTAS
 #define GLMX_EXACT_CTAS 3
 #endif
@@ -44,13 +47,13 @@ struct Cfg
     static constexpr int TB0 = 32 * K0, TB1 = 32 * K1;
     static constexpr int ROW0 = 8 * TB0, ROW1 = 8 * TB1;
     static constexpr int MAT = RB * (ROW0 > ROW1 ? ROW0 : ROW1);
-    static constexpr int XS = EXACT_MAXM * XROW;
+    static constexpr int XS = EXACT_MAXM * XSTR;
     static constexpr int STAGE = (MAT + XS + 127) / 128 * 128;   // tensor copies land 128-byte aligned
     static constexpr int NST = RING_BYTES / STAGE < 3 ? 3 : (RING_BYTES / STAGE > 12 ? 12 : RING_BYTES / STAGE);
     static constexpr int RED = NMAT * EXACT_MAXM * 128 * 8;      // (hi, lo) pairs
     static constexpr int SMEM = NST * STAGE + RED + 2 * NST * 8;
     static_assert(STAGE % 128 == 0 && MAT % 128 == 0, "stage alignment");
-    static_assert(EXACT_MAXM == 4 || EXACT_MAXM == 8, "EXACT GEMV jobs of 4 or 8 rows");
+    static_assert(GLMX_EXACT_TC ? EXACT_MAXM == 8 : (EXACT_MAXM == 4 || EXACT_MAXM == 8), "EXACT GEMV job rows");
 };
 
 struct GemvArgs
@@ -113,7 +116,7 @@ __device__ __forceinline__ void stage_fma(const uint8_t* st, int row_bytes, int 
 #pragma unroll
         for (int i = 0; i < M; ++i)
         {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xr + i * XROW);
+            const uint4 xv = *reinterpret_cast<const uint4*>(xr + i * XSTR);
             blk[i][0] = __fadd_rn(blk[i][0], dot8(a[0], a[2], b[0], b[2], xv));
             blk[i][1] = __fadd_rn(blk[i][1], dot8(a[1], a[3], b[1], b[3], xv));
         }
@@ -190,6 +193,80 @@ __device__ __forceinline__ void item_consume(uint8_t* ring, uint64_t* full, uint
     }
 }
 
+#if GLMX_EXACT_TC
+// m16n8k16 f16 x f16 -> f32 with C = 0: one 16-input tile of 16 outputs against 8 tokens. The MMA aligns its addends to
+// the largest and truncates below about 24 bits, so each MMA starts from zero (the error stays relative to one tile's
+// products, with no bias carried along the K loop) and the tile sums are added on the CUDA cores in fp32.
+__device__ __forceinline__ void hmma0(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// One pipeline stage of one matrix, tensor-core form: lane (g, tq) of consumer warp w decodes its A fragments of tiles
+// (2rp, w) and (2rp + 1, w), loads token g's activations of both tiles (one 16-byte load: B fragments of the two MMAs)
+// and adds the two MMA results - outputs (g, g + 8) x tokens (2tq, 2tq + 1) - into its block sums.
+template <int K>
+__device__ __forceinline__ void stage_tc(const uint8_t* st, int row_bytes, int t_off, int x_off, const LaneDecode<K>& L,
+                                         const OnesFrag& ones, float blk[4])
+{
+#pragma unroll
+    for (int rp = 0; rp < RB / 2; ++rp)
+    {
+        uint32_t a[4], b[4];
+        decode_frag_tc<K>(st + t_off + (2 * rp) * row_bytes, L, ones, a);
+        decode_frag_tc<K>(st + t_off + (2 * rp + 1) * row_bytes, L, ones, b);
+        const uint4 xv = *reinterpret_cast<const uint4*>(st + x_off + rp * 64);
+        float d[4], e[4];
+        hmma0(d, a, xv.x, xv.y);
+        hmma0(e, b, xv.z, xv.w);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) blk[c] = __fadd_rn(__fadd_rn(blk[c], d[c]), e[c]);
+    }
+}
+
+// The k-stages of one item, tensor-core form (any job of <= 8 rows): per lane 4 (output, token) block sums, each fed
+// once per 128-input block into a (hi, lo) pair by Fast2Sum; the pairs go to red[mat][token][col].
+template <int K0, int K1, int NMAT>
+__device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, uint64_t* empty, float2* red, int kqs,
+                                                int& s, uint32_t& ph, volatile int* s_abort, int* err, int warp, int lane,
+                                                const LaneDecode<K0>& L0, const LaneDecode<K1>& L1, const OnesFrag& ones)
+{
+    using C = Cfg<K0, K1, NMAT>;
+    const int g = lane >> 2, tq = lane & 3;
+    const int x_off = C::MAT + g * XSTR + tq * 16;
+#pragma unroll 1
+    for (int m = 0; m < NMAT; ++m)
+    {
+        float hi[4] = {0.0f, 0.0f, 0.0f, 0.0f}, lo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+        for (int q = 0; q < kqs; ++q)
+        {
+            if (!*s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(err, ERR_TIMEOUT_FULL); *s_abort = 1; }
+            const uint8_t* st = ring + s * C::STAGE;
+            float blk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (NMAT == 1 || m == 0) stage_tc<K0>(st, C::ROW0, warp * C::TB0, x_off, L0, ones, blk);
+            else stage_tc<K1>(st, C::ROW1, warp * C::TB1, x_off, L1, ones, blk);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == C::NST) { s = 0; ph ^= 1u; }
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+            {
+                const float sum = __fadd_rn(hi[c], blk[c]);
+                lo[c] = __fadd_rn(lo[c], __fsub_rn(blk[c], __fsub_rn(sum, hi[c])));
+                hi[c] = sum;
+            }
+        }
+        float2* rm = red + m * EXACT_MAXM * 128;
+        const int o = warp * 16 + g;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) rm[(2 * tq + (c & 1)) * 128 + o + 8 * (c >> 1)] = make_float2(hi[c], lo[c]);
+    }
+}
+#endif
+
 // EXACT-mode GEMV (one persistent kernel per phase). Items (job, 128-column block, K split); per item the producer
 // warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per row), the 8
 // consumer warps decode and multiply-accumulate on the CUDA cores (dot8, stage_fma) - the tensor pipe only forms the
@@ -250,7 +327,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
                     // the stage's RB k-tile rows x 8 tiles of the matrix: one tensor copy (x in 32-bit words)
                     tma_load_2d(st, map, nbi * 8 * tb / 4, kr, &full[s]);
                     for (int i = 0; i < job.z; ++i)
-                        bulk_g2s(st + C::MAT + i * XROW, xin + (size_t) (job.y + i) * a.kdim + kr * 16, XROW, &full[s]);
+                        bulk_g2s(st + C::MAT + i * XSTR, xin + (size_t) (job.y + i) * a.kdim + kr * 16, XROW, &full[s]);
                     ++issued;
                     if (++s == C::NST) { s = 0; ph ^= 1u; }
                 }
@@ -283,6 +360,9 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
         const int jn = item / S;
         const int nbi = jn % nb, j = jn / nb;
         const int4 job = a.jobs[j];
+#if GLMX_EXACT_TC
+        item_consume_tc<K0, K1, NMAT>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones);
+#else
         switch (job.z)
         {
             case 1: item_consume<K0, K1, NMAT, 1>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
@@ -296,6 +376,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 #endif
             default: item_consume<K0, K1, NMAT, EXACT_MAXM>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
         }
+#endif
         consumer_sync();
         if (S > 1)
         {
@@ -486,10 +567,20 @@ __device__ __forceinline__ void combine_cols(const CombineArgs& a, int t, int c)
     if (a.hc.x)
     {
         const float v[4] = { acc.x, acc.y, acc.z, acc.w };
+        float* xr = a.hc.x + (size_t) t * 4 * a.H;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            hc_apply_col(a.hc.x + (size_t) t * 4 * a.H, a.H, c + i, a.hc.y_half ? __half2float(__float2half_rn(v[i])) : v[i],
+            hc_apply_col(xr, a.H, c + i, a.hc.y_half ? __half2float(__float2half_rn(v[i])) : v[i],
                          a.hc.post + (size_t) t * 4, a.hc.comb + (size_t) t * 16);
+        if (a.hc.fn)
+        {
+            // the next site's mix partials of the updated stack: this warp's 32 quads are 128-column block c / 128
+            const size_t nb = a.H / 128, jb = c / 128;
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+                hc_mix_warp(*reinterpret_cast<const float4*>(xr + (size_t) g * a.H + c), a.hc.fn + (size_t) g * a.H + c,
+                            (size_t) 4 * a.H, a.hc.part + (((size_t) t * 4 + g) * nb + jb) * 25, threadIdx.x & 31);
+        }
         return;
     }
     const size_t o = (size_t) t * a.H + c;

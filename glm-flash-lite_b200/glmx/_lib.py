@@ -44,6 +44,7 @@ class GlmxError(RuntimeError):
 EXPORTS = ("glmx_version", "glmx_last_error", "glmx_layer_create", "glmx_layer_destroy", "glmx_layer_set_act_limit",
            "glmx_workspace_bytes", "glmx_route", "glmx_workspace_array", "glmx_moe_forward", "glmx_moe_forward_timed",
            "glmx_decode_tiles", "glmx_check", "glmx_moe_forward_noalloc", "glmx_moe_forward_hc",
+           "glmx_moe_forward_hc_mix", "glmx_hc_apply_partials", "glmx_hc_finalize_norm",
            "glmx_selftest_bounded_wait", "glmx_router", "glmx_moe_forward_peer", "glmx_peer_reduce", "glmx_ep_split", "glmx_ipc_alloc",
            "glmx_ipc_free", "glmx_ipc_handle", "glmx_ipc_open", "glmx_ipc_close", "glmx_layer_device", "glmx_check_noalloc",
            "glmx_ep_pack", "glmx_ep_unpack_add")
@@ -96,6 +97,14 @@ def load(path: str = LIB_PATH):
     L.glmx_layer_device.restype = _I
     L.glmx_moe_forward_hc.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _I, _P, C.c_size_t, _P]
     L.glmx_moe_forward_hc.restype = _I
+    L.glmx_moe_forward_hc_mix.argtypes = [_P, _P, _I, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, C.c_size_t,
+                                          _P]
+    L.glmx_moe_forward_hc_mix.restype = _I
+    L.glmx_hc_apply_partials.argtypes = [_P, _P, _I, _P, _P, _P, _P, _I, _I, _P]
+    L.glmx_hc_apply_partials.restype = _I
+    L.glmx_hc_finalize_norm.argtypes = [_P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P, C.c_float, C.c_float, _I, C.c_float,
+                                        C.c_float, C.c_float, _P]
+    L.glmx_hc_finalize_norm.restype = _I
     L.glmx_selftest_bounded_wait.argtypes = [_I, _P, _P]
     L.glmx_selftest_bounded_wait.restype = _I
     L.glmx_router.argtypes = [_P, _I, _I, _I, _P, _I, _P, _I, _I, _I, _I, _I, C.c_float, _P, _P, _I, _P, _I, _P]

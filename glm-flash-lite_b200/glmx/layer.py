@@ -179,10 +179,13 @@ class MoELayer:
         return out
 
     def forward_hc(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, hc_x: torch.Tensor, post: torch.Tensor,
-                   comb: torch.Tensor, y_half: bool = True, mode: int = _lib.MODE_I16, stream=None) -> torch.Tensor:
+                   comb: torch.Tensor, y_half: bool = True, mode: int = _lib.MODE_EXACT, stream=None,
+                   fn: torch.Tensor | None = None, partials: torch.Tensor | None = None) -> torch.Tensor:
         """The layer followed by the hyper-connection update of the MoE site (glmx_moe_forward_hc): hc_x fp32
         [ntok, 4, H] is updated in place with x_g <- post_g * y + sum_h comb[h][g] * x_h (y = the layer output, rounded
-        to fp16 first when y_half); post fp32 [ntok, 4], comb fp32 [ntok, 4, 4]. Returns hc_x."""
+        to fp16 first when y_half); post fp32 [ntok, 4], comb fp32 [ntok, 4, 4]. Returns hc_x.
+        With fn (fp16 [24, 4H]) and partials (fp32 [ntok, 4H/128, 25]) the next site's hc_mix_partials of the updated
+        stack are written too (glmx_moe_forward_hc_mix; the reference's apply_partials, glm53/k_hcfuse.py:296-320)."""
         x = x.contiguous(); sel = sel.contiguous(); w = w.contiguous()
         ntok = x.shape[0]
         topk = sel.shape[1] if sel.dim() == 2 else 0
@@ -192,10 +195,18 @@ class MoELayer:
         if post.shape != (ntok, 4) or comb.shape != (ntok, 4, 4):
             raise ValueError("post must be [ntok, 4] and comb [ntok, 4, 4]")
         ws = self.workspace(ntok, topk)
-        check(self.lib.glmx_moe_forward_hc(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
-                                           _dt(w), topk, int(mode), hc_x.data_ptr(), post.data_ptr(), comb.data_ptr(),
-                                           _lib.F16 if y_half else _lib.F32, ws.data_ptr(), ws.numel(),
-                                           _stream_ptr(stream)))
+        if fn is None:
+            check(self.lib.glmx_moe_forward_hc(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
+                                               _dt(w), topk, int(mode), hc_x.data_ptr(), post.data_ptr(), comb.data_ptr(),
+                                               _lib.F16 if y_half else _lib.F32, ws.data_ptr(), ws.numel(),
+                                               _stream_ptr(stream)))
+            return hc_x
+        from .hc import check_mix_args
+        check_mix_args(hc_x, fn, partials)
+        check(self.lib.glmx_moe_forward_hc_mix(self.h, x.data_ptr(), _dt(x), ntok, sel.data_ptr(), _dt(sel), w.data_ptr(),
+                                               _dt(w), topk, int(mode), hc_x.data_ptr(), post.data_ptr(), comb.data_ptr(),
+                                               _lib.F16 if y_half else _lib.F32, fn.data_ptr(), partials.data_ptr(),
+                                               ws.data_ptr(), ws.numel(), _stream_ptr(stream)))
         return hc_x
 
     def forward_peer(self, x: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, peer: "_lib.PeerOut",

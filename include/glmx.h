@@ -39,12 +39,13 @@ extern "C" {
 #define GLMX_I64 4
 
 /* numeric modes, same numbering as the reference's moe_forward (kernels/cpu_avx2/ft_core.h:822-823) */
-#define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights (GPU-exact), fp32 tensor-core accumulation */
+#define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights, exact fp16 products accumulated in fp32 (the decode GEMV
+                               with compensated block sums on the CUDA cores, the prefill GEMM on the tensor cores) */
 #define GLMX_MODE_I16 2     /* int16 activations per 128-block, exact integer tensor-core sums, the reference's fp32
                                flush order (ft_core.h:418-598): bit-identical to the reference's I16 mode. The decode
                                mode: at most 8192 rows (picks + shared-expert rows) per call */
 /* Path selection, OR'ed into the mode (EXACT only; default: chosen from the batch): GEMV = the decode kernels (one pass
- * over each expert's trellis per job of <= 8 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
+ * over each expert's trellis per job of <= 4 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
  * <= 128 rows, trellis decoded into shared memory once per 128-row tile), the default once the call has >= 12 rows per
  * expert on average. The reference's large-batch schedule is moe_forward_band (ft_core.h:1617-1651). */
 #define GLMX_PATH_GEMV 0x100
@@ -96,7 +97,8 @@ GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
 GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk);
 
 /* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
- * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward in I16 mode uses jobs of <= 4 rows). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
+ * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward uses jobs of <= 4 rows on its decode paths,
+ * <= 128 on the GEMM path). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
  * kernels/k110/ft_split_fast.cu:200-235) and the job grouping of moe_forward (kernels/cpu_avx2/ft_core.h:1344-1349).
  * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64) of global expert ids; ids outside
  * [first_expert, first_expert + E) are skipped (negative ids mask a pick).
@@ -141,6 +143,34 @@ GLMX_API int glmx_moe_forward_timed(const glmx_layer* layer, const void* x, int 
 GLMX_API int glmx_moe_forward_hc(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
                      int sel_dtype, const void* w, int w_dtype, int topk, int mode, float* hc_x, const float* hc_post,
                      const float* hc_comb, int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* glmx_moe_forward_hc followed by the next site's hc_mix_partials of the updated stream stack, as the reference's
+ * k_apply_partials does after its hc_apply (glm53/k_hcfuse.py:92-126; replaces ext().apply_partials(x, y, post, comb,
+ * fn, partials) with y = this layer's output, glm53/k_hcfuse.py:296-320, called at 427-428): fn fp16 [24][4H] (16-byte aligned), partials fp32
+ * [ntok][4H/128][25]: for row t, stream g and 128-column block b the 25 sums at (t*4H/128 + g*H/128 + b)*25 - the 24
+ * products s.fn_j and s.s over the block's updated values, bit-identical to the reference's reduction tree. On the EXACT
+ * GEMV path this runs inside the combine kernel; the I16 and GEMM paths add one pass over the updated stack. */
+GLMX_API int glmx_moe_forward_hc_mix(const glmx_layer* layer, const void* x, int x_dtype, int ntok, const void* sel,
+                     int sel_dtype, const void* w, int w_dtype, int topk, int mode, float* hc_x, const float* hc_post,
+                     const float* hc_comb, int y_dtype, const uint16_t* fn, float* partials, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* The reference's fused site kernels on their own (replace ext().apply_partials and ext().finalize_norm,
+ * glm53/k_hcfuse.py:296-344, called at 427-432). glmx_hc_apply_partials: with y (fp16 or fp32 [R][D]) the hc_apply update of x fp32
+ * [R][4][D] in place (post [R][4], comb [R][4][4]), then the mix partials of the (updated) stack into partials
+ * [R][4D/128][25]; y == NULL computes only the partials. D a multiple of 128. Bit-identical to the reference. */
+GLMX_API int glmx_hc_apply_partials(float* x, const void* y, int y_dtype, const float* post, const float* comb,
+                     const uint16_t* fn, float* partials, int R, int D, void* stream);
+
+/* hc_mix_finalize + the site's RMSNorm (glm53/k_hcfuse.py:129-294): from the partials of glmx_hc_apply_partials, per
+ * row the 25 mix sums, rmr = rsqrt(mix[24] / 4D + rms_eps), post [R][4] = 2 sigmoid(mix[4+g] rmr scale[1] + base[4+g]),
+ * comb [R][4][4] by Sinkhorn (iters rounds, hc_eps) of mix[8+..] rmr scale[2] + base[8+..], and out fp16 [R][D] = the
+ * collapsed row sum_h (sigmoid(mix[h] rmr scale[0] + base[h]) + hc_eps) x_h (rounded to fp16, clamped) normalised by
+ * its RMS (n_eps) times cscale and (nw + cbias); nw fp16 or bf16 [D]. D a multiple of 512, at most 16384; for
+ * D = 4096 (the size the reference builds it for) bit-identical to the reference. */
+GLMX_API int glmx_hc_finalize_norm(const float* x, const float* partials, int R, int D, const float* base,
+                     const float* scale, float* post, float* comb, const void* nw, int nw_dtype, uint16_t* out,
+                     float rms_eps, float hc_eps, int iters, float n_eps, float cbias, float cscale, void* stream);
 
 /* Known-answer entry for the trellis decode: `ntiles` tiles of 32*bits bytes (device) -> fp16 bit patterns
  * [ntiles, 16, 16] (row r = input index, column c = output index), as dense_weights (kernels/cpu_avx2/ft_core.h:1657-1672). */

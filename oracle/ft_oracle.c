@@ -373,6 +373,111 @@ void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, con
         }
 }
 
+/* ---- hc_mix_partials (glm53/k_hcfuse.py:92-126): per-lane terms, then the warp's shfl_down tree ---- */
+void fto_hc_mix_partials(const float* x, const uint16_t* fn, int R, int D, float* part)
+{
+    const int nb = D / 128, nhalf = 4 * nb;
+    for (int r = 0; r < R; ++r)
+        for (int g = 0; g < 4; ++g)
+            for (int jb = 0; jb < nb; ++jb)
+            {
+                float v[32][25];
+                for (int l = 0; l < 32; ++l)
+                {
+                    const int q = jb * 32 + l;
+                    const float* s = x + (size_t) r * 4 * D + (size_t) g * D + 4 * q;
+                    float a = 0.0f;
+                    for (int i = 0; i < 4; ++i) a = fmaf(s[i], s[i], a);
+                    v[l][24] = a;
+                    for (int j = 0; j < 24; ++j)
+                    {
+                        const uint16_t* w = fn + (size_t) j * 4 * D + (size_t) g * D + 4 * q;
+                        const float d = fmaf(s[0], fto_h2f(w[0]), fmaf(s[1], fto_h2f(w[1]),
+                                             fmaf(s[2], fto_h2f(w[2]), s[3] * fto_h2f(w[3]))));
+                        v[l][j] = 0.0f + d;
+                    }
+                }
+                for (int off = 16; off > 0; off >>= 1)
+                    for (int l = 0; l < off; ++l)
+                        for (int k = 0; k < 25; ++k) v[l][k] = v[l][k] + v[l + off][k];
+                for (int k = 0; k < 25; ++k) part[((size_t) r * nhalf + (size_t) g * nb + jb) * 25 + k] = v[0][k];
+            }
+}
+
+static float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+void fto_hc_finalize_norm(const float* x, const float* part, int R, int D, const float* base, const float* scale,
+                          const float* nw, float rms_eps, float hc_eps, int iters, float n_eps, float cbias, float cscale,
+                          float* post, float* comb, uint16_t* out)
+{
+    const int chunks = 4 * D / 256, per = chunks / 8;
+    for (int r = 0; r < R; ++r)
+    {
+        const float* p = part + (size_t) r * 2 * chunks * 25;
+        float mix[25];
+        for (int k = 0; k < 25; ++k)
+        {
+            float tot = 0.0f;
+            for (int w = 0; w < 8; ++w)
+            {
+                float v = 0.0f;
+                for (int i = 0; i < per; ++i)
+                {
+                    const int c = w + 8 * i;
+                    v += (0.0f + p[(size_t) 2 * c * 25 + k]) + p[(size_t) (2 * c + 1) * 25 + k];
+                }
+                tot += v;
+            }
+            mix[k] = tot;
+        }
+        const float rmr = 1.0f / sqrtf(mix[24] / (float) (4 * D) + rms_eps);
+        for (int g = 0; g < 4; ++g) post[r * 4 + g] = 2.0f * sigmoid_f(fmaf(mix[4 + g] * rmr, scale[1], base[4 + g]));
+        float v[16];
+        for (int t = 0; t < 16; ++t) v[t] = fmaf(mix[8 + t] * rmr, scale[2], base[8 + t]);
+        for (int h = 0; h < 4; ++h)
+        {
+            float m = v[h * 4];
+            for (int g = 1; g < 4; ++g) m = fmaxf(m, v[h * 4 + g]);
+            float s = 0.0f;
+            for (int g = 0; g < 4; ++g) { v[h * 4 + g] = expf(v[h * 4 + g] - m); s += v[h * 4 + g]; }
+            for (int g = 0; g < 4; ++g) v[h * 4 + g] = v[h * 4 + g] / s + hc_eps;
+        }
+        for (int it = 0; it < iters; ++it)
+        {
+            if (it > 0)
+                for (int h = 0; h < 4; ++h)
+                {
+                    float rs = 0.0f;
+                    for (int g = 0; g < 4; ++g) rs += v[h * 4 + g];
+                    for (int g = 0; g < 4; ++g) v[h * 4 + g] /= rs + hc_eps;
+                }
+            for (int g = 0; g < 4; ++g)
+            {
+                float cs = 0.0f;
+                for (int h = 0; h < 4; ++h) cs += v[h * 4 + g];
+                for (int h = 0; h < 4; ++h) v[h * 4 + g] /= cs + hc_eps;
+            }
+        }
+        memcpy(comb + (size_t) r * 16, v, sizeof v);
+        float pre[4];
+        for (int h = 0; h < 4; ++h) pre[h] = sigmoid_f(fmaf(mix[h] * rmr, scale[0], base[h])) + hc_eps;
+        float* col = malloc(sizeof(float) * (size_t) D);
+        double ss = 0.0;
+        for (int c = 0; c < D; ++c)
+        {
+            float o = 0.0f;
+            for (int h = 0; h < 4; ++h) o = fmaf(pre[h], x[(size_t) r * 4 * D + (size_t) h * D + c], o);
+            o = r16(o);
+            o = fmaxf(-65504.0f, fminf(o, 65504.0f));
+            col[c] = o;
+            ss += (double) o * o;
+        }
+        const float rmf = 1.0f / sqrtf((float) ss / (float) D + n_eps) * cscale;
+        for (int c = 0; c < D; ++c) out[(size_t) r * D + c] = fto_f2h(col[c] * (nw[c] + cbias) * rmf);
+        free(col);
+    }
+}
+
 /* ---- router in front of the split (the GLM-4 MoE routing of exllamav3's router, as transformers states it in
  * models/glm4_moe/modeling_glm4_moe.py:302-305 (gate) and 389-412 (route_tokens_to_experts)) ---- */
 

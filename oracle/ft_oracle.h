@@ -91,6 +91,23 @@ void fto_moe_forward(const fto_expert_t* experts, int E, const fto_expert_t* sha
  * post [R][4], comb [R][4][4] (comb[h][g]): x_g <- fma(comb[3][g], x_3, ... fma(comb[0][g], x_0, post_g * y)). */
 void fto_hc_apply(float* x, const float* y, int R, int D, const float* post, const float* comb);
 
+/* hc_mix_partials of the next site (glm53/k_hcfuse.py:92-126): for row r, stream g and 128-column block jb, the 25
+ * sums over the block's 32 column quads (lane l = quad jb*32 + l) of s.fn_j (j < 24, fn [24][4D] fp16, 4-term fma
+ * chain from s.w*w.w) and of s.s (fma chain from 0), each reduced over the 32 lanes by the warp's shfl_down tree.
+ * part [R][4 D/128][25], index (r * 4 D/128 + g * D/128 + jb) * 25 + k. */
+void fto_hc_mix_partials(const float* x, const uint16_t* fn, int R, int D, float* part);
+
+/* hc_mix_finalize + RMSNorm of the collapsed row (glm53/k_hcfuse.py:129-294), in plain fp32 math (expf, 1/sqrtf,
+ * IEEE division: the reference's fast intrinsics are not restated, so this is a tolerance check): mix = the chunk sums
+ * of part (chunk k = (0 + half 2k) + half 2k+1, warp w sums chunks w, w+8, ..., then the 8 warps in order);
+ * rmr = 1/sqrt(mix[24] / 4D + rms_eps); post = 2 sigmoid(mix[4+g] rmr scale[1] + base[4+g]); comb = Sinkhorn
+ * (softmax over g per h, + hc_eps, column-normalised, iters - 1 more row/column rounds) of mix[8+4h+g] rmr scale[2] +
+ * base[8+4h+g]; pre = sigmoid(mix[h] rmr scale[0] + base[h]) + hc_eps; out = fp16(c * (nw + cbias) * rmf) with
+ * c = clamp(fp16(sum_h pre_h x_h)) and rmf = cscale / sqrt(sum c^2 / D + n_eps). nw fp32 values [D]. */
+void fto_hc_finalize_norm(const float* x, const float* part, int R, int D, const float* base, const float* scale,
+                          const float* nw, float rms_eps, float hc_eps, int iters, float n_eps, float cbias, float cscale,
+                          float* post, float* comb, uint16_t* out);
+
 /* Router in front of the split: the GLM-4 MoE routing of exllamav3's router (un-vendored third-party code), as the
  * published model code states it (transformers, models/glm4_moe/modeling_glm4_moe.py:302-305 and 389-412).
  * fto_router_gate: logits[t][e] = sum_h z[t][h] * W[e][h], accumulated in fp64 and rounded once (the reference

@@ -68,6 +68,8 @@ class Oracle:
         L.fto_moe_forward.argtypes = [_P, _I, _P, _I, _I, _I, _F, _P, _I, _P, _P, _I, _P]
         L.fto_expert_i16.argtypes = [_P, _I, _I, _F, _P, _I, _P]
         L.fto_hc_apply.argtypes = [_P, _P, _I, _I, _P, _P]
+        L.fto_hc_mix_partials.argtypes = [_P, _P, _I, _I, _P]
+        L.fto_hc_finalize_norm.argtypes = [_P, _P, _I, _I, _P, _P, _P, _F, _F, _I, _F, _F, _F, _P, _P, _P]
         L.fto_router_gate.argtypes = [_P, _I, _I, _P, _I, _P]
         L.fto_router_sigmoid.argtypes = [_P, _I, _P]
         L.fto_router_select.argtypes = [_P, _I, _I, _P, _I, _I, _I, _I, _F, _P, _P]
@@ -99,6 +101,28 @@ class Oracle:
         self.L.fto_hc_apply(_ptr(x), _ptr(np.ascontiguousarray(y, np.float32)), R, D,
                             _ptr(np.ascontiguousarray(post, np.float32)), _ptr(np.ascontiguousarray(comb, np.float32)))
         return x
+
+    def hc_mix_partials(self, x: np.ndarray, fn: np.ndarray) -> np.ndarray:
+        """hc_mix_partials (fto_hc_mix_partials): stream stack x [R, 4, D] fp32, fn [24, 4D] fp16 -> [R, 4D/128, 25]."""
+        x = np.ascontiguousarray(x, np.float32)
+        R, _, D = x.shape
+        fn = np.ascontiguousarray(fn, np.float16).view(np.uint16)
+        part = np.empty((R, 4 * D // 128, 25), np.float32)
+        self.L.fto_hc_mix_partials(_ptr(x), _ptr(fn), R, D, _ptr(part))
+        return part
+
+    def hc_finalize_norm(self, x, part, base, scale, nw, rms_eps, hc_eps, iters, n_eps, cbias, cscale):
+        """hc_mix_finalize + RMSNorm in plain fp32 math (fto_hc_finalize_norm) -> (post [R,4], comb [R,4,4], out fp16 [R,D])."""
+        x = np.ascontiguousarray(x, np.float32)
+        R, _, D = x.shape
+        post = np.empty((R, 4), np.float32)
+        comb = np.empty((R, 4, 4), np.float32)
+        out = np.empty((R, D), np.uint16)
+        c = lambda a: np.ascontiguousarray(a, np.float32)
+        part, base, scale, nw = c(part), c(base), c(scale), c(nw)
+        self.L.fto_hc_finalize_norm(_ptr(x), _ptr(part), R, D, _ptr(base), _ptr(scale), _ptr(nw), rms_eps, hc_eps,
+                                    int(iters), n_eps, cbias, cscale, _ptr(post), _ptr(comb), _ptr(out))
+        return post, comb, out.view(np.float16)
 
     # --- router ----------------------------------------------------------------------------------------------
     def router_gate(self, z: np.ndarray, W: np.ndarray) -> np.ndarray:

@@ -1,6 +1,6 @@
 """Pins the CPU restatement (oracle/ft_oracle.c) against fixtures produced by the reference's own ft_core.h
-(tests/golden/make_golden.py), and the router restatement against the published GLM-4 MoE routing
-(tests/golden/make_router_golden.py). CPU only."""
+(tests/golden/make_golden.py) and by the reference's own hyper-connection kernels (tests/golden/make_hc_golden.py),
+and the router restatement against the published GLM-4 MoE routing (tests/golden/make_router_golden.py). CPU only."""
 import sys
 
 import numpy as np
@@ -103,6 +103,47 @@ def test_hc_apply_restatement(oracle):
         np.einsum("rhg,rhd->rgd", comb.astype(np.float64), x.astype(np.float64))
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
     np.testing.assert_array_equal(x, oracle.hc_apply(x, y, post, comb) * 0 + x)      # input untouched
+
+
+@pytest.mark.parametrize("case", ["apply_h", "apply_f"])
+def test_hc_apply_pinned_to_reference_kernel(oracle, case):
+    """fto_hc_apply equals the stream-stack update of the reference's own k_apply_partials (glm53/k_hcfuse.py:62-91,
+    run by tests/golden/make_hc_golden.py) bit for bit, y given as fp16 and as fp32."""
+    d = load_golden("hc_ref")
+    got = oracle.hc_apply(d[f"{case}_x"], d[f"{case}_y"], d[f"{case}_post"], d[f"{case}_comb"])
+    np.testing.assert_array_equal(got, d[f"{case}_xout"])
+
+
+@pytest.mark.parametrize("case", ["apply_h", "apply_f", "mix_only", "final_h", "final_b"])
+def test_hc_mix_partials_pinned_to_reference_kernel(oracle, case):
+    """fto_hc_mix_partials equals the reference's hc_mix_partials (k_apply_partials, glm53/k_hcfuse.py:92-126) bit for
+    bit, on the stack after its update (or as given, mix only)."""
+    d = load_golden("hc_ref")
+    stack = d[f"{case}_xout"] if f"{case}_xout" in d else d[f"{case}_x"]
+    if case.startswith("final"):
+        sys.path.insert(0, GOLDEN)
+        import make_hc_golden as M
+        c = [f for f in M.FINAL_CASES if f[0] == case][0]
+        fn = M.inputs_final(c[1], c[2], c[6])[1]
+    else:
+        fn = d[f"{case}_fn"]
+    np.testing.assert_array_equal(oracle.hc_mix_partials(stack, fn), d[f"{case}_part"])
+
+
+@pytest.mark.parametrize("case", ["final_h", "final_b"])
+def test_hc_finalize_restatement_vs_reference_kernel(oracle, case):
+    """fto_hc_finalize_norm (plain fp32 math) against the reference's finalize_norm (fast intrinsics: __expf,
+    __fdividef, rsqrtf, a few ulp each, 20 Sinkhorn rounds): post and comb within 1e-5 relative, the normalised fp16
+    row within two fp16 steps of the reference's value (one rounding flip, which may cross a binade)."""
+    d = load_golden("hc_ref")
+    rms_eps, hc_eps, iters, n_eps, cbias, cscale = d[f"{case}_args"].tolist()
+    post, comb, out = oracle.hc_finalize_norm(d[f"{case}_x"], d[f"{case}_part"], d[f"{case}_base"], d[f"{case}_scale"],
+                                              d[f"{case}_nw"], rms_eps, hc_eps, int(iters), n_eps, cbias, cscale)
+    np.testing.assert_allclose(post, d[f"{case}_post"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(comb, d[f"{case}_comb"], rtol=1e-5, atol=1e-7)
+    ref = d[f"{case}_out"].astype(np.float32)
+    step = np.abs(np.spacing(ref.astype(np.float16))).astype(np.float32)
+    assert np.all(np.abs(out.astype(np.float32) - ref) <= 2 * step)
 
 
 def _router_case(name):
