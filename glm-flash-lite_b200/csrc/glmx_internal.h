@@ -135,13 +135,7 @@ cudaError_t launch_hc_finalize(const float* x, const float* part, const float* b
                                float hc_eps, int iters, float n_eps, float cbias, float cscale, cudaStream_t st);
 
 constexpr int I16_MAXM = 4;            // rows per job in I16 mode (one 4-token activation set)
-#ifndef GLMX_EXACT_TC
-#define GLMX_EXACT_TC 0            // 1: EXACT GEMV dot products as tensor-core MMAs from zero per 16-input tile
-#endif
-#ifndef GLMX_EXACT_MAXM
-#define GLMX_EXACT_MAXM (GLMX_EXACT_TC ? 8 : 4)
-#endif
-constexpr int EXACT_MAXM = GLMX_EXACT_MAXM;   // rows per job of the EXACT decode GEMV (per-row accumulators in registers)
+constexpr int EXACT_MAXM = 8;         // rows per job of the EXACT decode GEMV (the 8 token columns of one MMA)
 constexpr int I16_ACT_BYTES = 4096;    // replicated activation planes of one (job, projection, 128-input block)
 // one (job, 128-input block) record of the I16 activations, laid out as a GEMV stage holds it: the nmat projections'
 // planes, then their 4 scales (16 bytes each)

@@ -3,9 +3,9 @@
 // Pipeline of one forward call (all on one stream):
 //   route   (route.cu)        picks -> expert-major rows, jobs of <= 8 rows
 //   prep                      per row: xt = fp16(had128(x * suh) * HAD) for gate and up   (ft_core.h:96-102)
-//   gemv<gate+up>             per (job, 128-col block, k-split): trellis tiles streamed by the bulk-copy engine into a
-//                             shared-memory ring, decoded in registers straight into mma.m16n8k16 A fragments, fp32
-//                             accumulation; epilogue: out_block (ft_core.h:104-110) of g and u, a = fp16(silu(g) * u)
+//   gemv<gate+up>             per (job, 128-col block, k-split): trellis tiles streamed by the tensor-copy engine into
+//                             a shared-memory ring, decoded in registers straight into mma.m16n8k16 A fragments (one
+//                             MMA per tile from zero, tile sums added in fp32, compensated per block); epilogue: out_block (ft_core.h:104-110) of g and u, a = fp16(silu(g) * u)
 //                             (ft_core.h:123-132, 980), then the down projection's input transform for that block
 //   gemv<down>                same main loop over the down matrix; epilogue out_block -> per-row fp32 y
 //   combine                   out[t] = sum over t's picks in pick order of w * y (+ shared expert), fp32
@@ -30,9 +30,9 @@ constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
 constexpr int XROW = 256;    // bytes per staged activation row: one 128-input block, fp16, in the lane order of gemv_xpos
-// stride of the staged activation rows in a stage: the tensor-core form reads row g at lane (g, tq), and a 320-byte
-// stride puts the two rows of each quarter-warp's 16-byte loads in different bank halves
-constexpr int XSTR = GLMX_EXACT_TC ? 320 : XROW;
+// stride of the staged activation rows in a stage: lane (g, tq) reads row g, and a 320-byte stride puts the two rows
+// of each quarter-warp's 16-byte loads in different bank halves
+constexpr int XSTR = 320;
 #ifndef GLMX_EXACT_CTAS
 #define GLMX_EXACT_CTAS 3
 #endif
@@ -53,7 +53,7 @@ struct Cfg
     static constexpr int RED = NMAT * EXACT_MAXM * 128 * 8;      // (hi, lo) pairs
     static constexpr int SMEM = NST * STAGE + RED + 2 * NST * 8;
     static_assert(STAGE % 128 == 0 && MAT % 128 == 0, "stage alignment");
-    static_assert(GLMX_EXACT_TC ? EXACT_MAXM == 8 : (EXACT_MAXM == 4 || EXACT_MAXM == 8), "EXACT GEMV job rows");
+    static_assert(EXACT_MAXM == 8, "EXACT GEMV jobs of up to 8 rows: the 8 token columns of one MMA");
 };
 
 struct GemvArgs
@@ -78,122 +78,6 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
 
-// 8-term partial dot product of a lane's two tile rows (2rp, 2rp+1) with one token, in fp32 with exact fp16 x fp16
-// products: a chain of mixed-precision FMAs (fp16 operands, fp32 accumulate, one rounding each) starting from zero,
-// row 2rp's four terms (weights w01 = (w0, w1), w23 = (w2, w3) against x.x, x.y) then row 2rp+1's (v01, v23 against
-// x.z, x.w).
-__device__ __forceinline__ float dot8(uint32_t w01, uint32_t w23, uint32_t v01, uint32_t v23, uint4 xv)
-{
-    float d;
-    asm("{\n .reg .f16 a0, a1, a2, a3, b0, b1, b2, b3, x0, x1, x2, x3, x4, x5, x6, x7;\n"
-        " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {b0, b1}, %3;\n mov.b32 {b2, b3}, %4;\n"
-        " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
-        " fma.rn.f32.f16 %0, a0, x0, 0f00000000;\n fma.rn.f32.f16 %0, a1, x1, %0;\n"
-        " fma.rn.f32.f16 %0, a2, x2, %0;\n fma.rn.f32.f16 %0, a3, x3, %0;\n"
-        " fma.rn.f32.f16 %0, b0, x4, %0;\n fma.rn.f32.f16 %0, b1, x5, %0;\n"
-        " fma.rn.f32.f16 %0, b2, x6, %0;\n fma.rn.f32.f16 %0, b3, x7, %0;\n}"
-        : "=f"(d)
-        : "r"(w01), "r"(w23), "r"(v01), "r"(v23), "r"(xv.x), "r"(xv.y), "r"(xv.z), "r"(xv.w));
-    return d;
-}
-
-// One pipeline stage of one matrix for an M-row job. Lane (g, tq) of consumer warp w decodes its 8 weights of tiles
-// (2rp, w) and (2rp + 1, w) (decode_frag_tc: output columns g and g + 8, input rows PERM16(2tq), PERM16(2tq+1) and the
-// same + 8), forms for each row of the job the 8-term partial of each of its two columns and adds it into that
-// column's block sum. The lane's activations of the two tile rows are one 16-byte load (gemv_xpos); the four quads'
-// loads fill one 64-byte run.
-template <int K, int M>
-__device__ __forceinline__ void stage_fma(const uint8_t* st, int row_bytes, int t_off, int x_off, const LaneDecode<K>& L,
-                                          const OnesFrag& ones, float blk[M][2])
-{
-#pragma unroll
-    for (int rp = 0; rp < RB / 2; ++rp)
-    {
-        uint32_t a[4], b[4];
-        decode_frag_tc<K>(st + t_off + (2 * rp) * row_bytes, L, ones, a);
-        decode_frag_tc<K>(st + t_off + (2 * rp + 1) * row_bytes, L, ones, b);
-        const uint8_t* xr = st + x_off + rp * 64;
-#pragma unroll
-        for (int i = 0; i < M; ++i)
-        {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xr + i * XSTR);
-            blk[i][0] = __fadd_rn(blk[i][0], dot8(a[0], a[2], b[0], b[2], xv));
-            blk[i][1] = __fadd_rn(blk[i][1], dot8(a[1], a[3], b[1], b[3], xv));
-        }
-    }
-}
-
-// Sum of the four lanes (tq = 0..3) of a quad of (hi, lo) pairs: TwoSum of the hi parts (exact error term), lo parts
-// added; every lane of the quad ends with the same pair.
-__device__ __forceinline__ void quad_sum(float& h, float& l)
-{
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1)
-    {
-        const float h2 = __shfl_xor_sync(0xffffffffu, h, off), l2 = __shfl_xor_sync(0xffffffffu, l, off);
-        const float s = __fadd_rn(h, h2);
-        const float bb = __fsub_rn(s, h);
-        const float e = __fadd_rn(__fsub_rn(h, __fsub_rn(s, bb)), __fsub_rn(h2, bb));
-        l = __fadd_rn(__fadd_rn(l, l2), e);
-        h = s;
-    }
-}
-
-// The k-stages of one item for an M-row job: matrix by matrix, each lane keeps per (row, column) a block sum (fp32)
-// and a running (hi, lo) pair fed once per 128-input block by Fast2Sum, so the rounding error stays at the level of
-// one 128-input block; at the end the quad's pairs are summed (quad_sum) and the pair goes to red[mat][row][col].
-template <int K0, int K1, int NMAT, int M>
-__device__ __forceinline__ void item_consume(uint8_t* ring, uint64_t* full, uint64_t* empty, float2* red, int kqs,
-                                             int& s, uint32_t& ph, volatile int* s_abort, int* err, int warp, int lane,
-                                             const LaneDecode<K0>& L0, const LaneDecode<K1>& L1, const OnesFrag& ones)
-{
-    using C = Cfg<K0, K1, NMAT>;
-    const int g = lane >> 2, tq = lane & 3;
-    const int x_off = C::MAT + tq * 16;
-#pragma unroll 1
-    for (int m = 0; m < NMAT; ++m)
-    {
-        float hi[M][2], lo[M][2];
-#pragma unroll
-        for (int i = 0; i < M; ++i) hi[i][0] = hi[i][1] = lo[i][0] = lo[i][1] = 0.0f;
-#pragma unroll 1
-        for (int q = 0; q < kqs; ++q)
-        {
-            if (!*s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(err, ERR_TIMEOUT_FULL); *s_abort = 1; }
-            const uint8_t* st = ring + s * C::STAGE;
-            float blk[M][2];
-#pragma unroll
-            for (int i = 0; i < M; ++i) blk[i][0] = blk[i][1] = 0.0f;
-            if (NMAT == 1 || m == 0) stage_fma<K0, M>(st, C::ROW0, warp * C::TB0, x_off, L0, ones, blk);
-            else stage_fma<K1, M>(st, C::ROW1, warp * C::TB1, x_off, L1, ones, blk);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == C::NST) { s = 0; ph ^= 1u; }
-#pragma unroll
-            for (int i = 0; i < M; ++i)
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-                {
-                    const float sum = __fadd_rn(hi[i][c], blk[i][c]);
-                    lo[i][c] = __fadd_rn(lo[i][c], __fsub_rn(blk[i][c], __fsub_rn(sum, hi[i][c])));
-                    hi[i][c] = sum;
-                }
-        }
-        float2* rm = red + m * EXACT_MAXM * 128;
-        const int o = warp * 16 + g;
-#pragma unroll
-        for (int i = 0; i < M; ++i)
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-            {
-                float h = hi[i][c], l = lo[i][c];
-                quad_sum(h, l);
-                if (tq == 0) rm[i * 128 + o + 8 * c] = make_float2(h, l);
-            }
-    }
-}
-
-#if GLMX_EXACT_TC
 // m16n8k16 f16 x f16 -> f32 with C = 0: one 16-input tile of 16 outputs against 8 tokens. The MMA aligns its addends to
 // the largest and truncates below about 24 bits, so each MMA starts from zero (the error stays relative to one tile's
 // products, with no bias carried along the K loop) and the tile sums are added on the CUDA cores in fp32.
@@ -265,13 +149,12 @@ __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, u
         for (int c = 0; c < 4; ++c) rm[(2 * tq + (c & 1)) * 128 + o + 8 * (c >> 1)] = make_float2(hi[c], lo[c]);
     }
 }
-#endif
 
-// EXACT-mode GEMV (one persistent kernel per phase). Items (job, 128-column block, K split); per item the producer
-// warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per row), the 8
-// consumer warps decode and multiply-accumulate on the CUDA cores (dot8, stage_fma) - the tensor pipe only forms the
-// trellis byte sums, whose integer results are exact. The hardware MMA's fp32 accumulation is not used for the dot
-// products: it truncates the aligned sum of each MMA to about the precision of its largest addend.
+// EXACT-mode GEMV (one persistent kernel per phase). Items (job of <= 8 rows, 128-column block, K split); per item the
+// producer warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per
+// row), the 8 consumer warps decode (byte sums on the integer tensor pipe, codebook by HFMA2) and form each 16x16 tile's
+// products with one m16n8k16 MMA against the job's 8 token columns, started from zero (stage_tc); the tile sums are
+// added on the CUDA cores, block sums compensated (Fast2Sum, TwoSum across K splits).
 template <int K0, int K1, int NMAT, bool GATEUP>
 __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 {
@@ -293,6 +176,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
     }
     __syncthreads();
 
+    pdl_enter();                  // the split's plan and jobs and the staged activations come from earlier kernels
     const Plan pl = *a.plan;
     const int nb = a.ntn / 8;
     const int S = GATEUP ? pl.S_gu : pl.S_d;
@@ -360,23 +244,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
         const int jn = item / S;
         const int nbi = jn % nb, j = jn / nb;
         const int4 job = a.jobs[j];
-#if GLMX_EXACT_TC
         item_consume_tc<K0, K1, NMAT>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones);
-#else
-        switch (job.z)
-        {
-            case 1: item_consume<K0, K1, NMAT, 1>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-            case 2: item_consume<K0, K1, NMAT, 2>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-            case 3: item_consume<K0, K1, NMAT, 3>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-#if GLMX_EXACT_MAXM > 4
-            case 4: item_consume<K0, K1, NMAT, 4>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-            case 5: item_consume<K0, K1, NMAT, 5>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-            case 6: item_consume<K0, K1, NMAT, 6>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-            case 7: item_consume<K0, K1, NMAT, 7>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-#endif
-            default: item_consume<K0, K1, NMAT, EXACT_MAXM>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones); break;
-        }
-#endif
         consumer_sync();
         if (S > 1)
         {
@@ -491,6 +359,7 @@ __device__ __forceinline__ float load_x(const void* x, int dt, size_t i)
 
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
 {
+    pdl_enter();
     const int nbk = a.H / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -605,6 +474,7 @@ __device__ __forceinline__ void combine_cols(const CombineArgs& a, int t, int c)
 
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a)
 {
+    pdl_enter();
     const int t = blockIdx.y;
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (c < a.H) combine_cols(a, t, c);
@@ -648,8 +518,7 @@ cudaError_t launch_gemv(const Layer& L, const GemvArgs& a, int grid, cudaStream_
         if (e != cudaSuccess) return e;
         attr_set[L.device] = true;
     }
-    gemv_kernel<K0, K1, NMAT, GATEUP><<<grid, NTHR, C::SMEM, st>>>(a);
-    return cudaGetLastError();
+    return launch_chained(gemv_kernel<K0, K1, NMAT, GATEUP>, dim3(grid), dim3(NTHR), C::SMEM, st, a);
 }
 
 template <int K0>
@@ -762,8 +631,7 @@ cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, int nt
     p.xu = reinterpret_cast<__half*>(ws + lay.xu);
     p.natural = natural ? 1 : 0;
     const long long warps = (long long) ntok * 2 * (L.H / 128);
-    prep_kernel<<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return launch_chained(prep_kernel, dim3((unsigned) ((warps + 7) / 8)), dim3(256), 0, st, p);
 }
 
 cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, int ntok, int topk, int mode, void* out,
@@ -828,8 +696,7 @@ cudaError_t launch_decode_forward(const Layer& L, const void* x, int x_dtype, in
         c.out = out; c.out_dtype = out_dtype; c.accumulate = accumulate;
         c.hc = hc ? *hc : HcOut{ nullptr, nullptr, nullptr, 0 };
         dim3 grd((unsigned) ((L.H / 4 + 255) / 256), (unsigned) ntok);
-        combine_kernel<<<grd, 256, 0, st>>>(c);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_chained(combine_kernel, grd, dim3(256), 0, st, c)) != cudaSuccess) return e;
     }
     return mark(5);
 }

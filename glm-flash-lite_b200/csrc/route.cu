@@ -29,7 +29,7 @@ struct RouteArgs
     const void* w; int w_dtype;
     int ntok, topk, E, has_shared;
     int first;                // global id of local expert 0
-    int maxm;                 // rows per job (8 EXACT, 4 I16)
+    int maxm;                 // rows per job (EXACT GEMV 8, I16 4, GEMM 128)
     int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
     int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
     int grid_ctas, part_slots;

@@ -39,13 +39,14 @@ extern "C" {
 #define GLMX_I64 4
 
 /* numeric modes, same numbering as the reference's moe_forward (kernels/cpu_avx2/ft_core.h:822-823) */
-#define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights, exact fp16 products accumulated in fp32 (the decode GEMV
-                               with compensated block sums on the CUDA cores, the prefill GEMM on the tensor cores) */
+#define GLMX_MODE_EXACT 1   /* fp16-rounded codebook weights, fp16 x fp16 products accumulated in fp32 (decode GEMV:
+                               one tensor-core MMA per 16x16 tile started from zero, tile sums added in fp32 with
+                               compensated block sums; prefill GEMM: short tensor-memory accumulation chains) */
 #define GLMX_MODE_I16 2     /* int16 activations per 128-block, exact integer tensor-core sums, the reference's fp32
                                flush order (ft_core.h:418-598): bit-identical to the reference's I16 mode. The decode
                                mode: at most 8192 rows (picks + shared-expert rows) per call */
 /* Path selection, OR'ed into the mode (EXACT only; default: chosen from the batch): GEMV = the decode kernels (one pass
- * over each expert's trellis per job of <= 4 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
+ * over each expert's trellis per job of <= 8 rows); GEMM = the prefill kernels (tcgen05 tensor-core GEMM over jobs of
  * <= 128 rows, trellis decoded into shared memory once per 128-row tile), the default once the call has >= 12 rows per
  * expert on average. The reference's large-batch schedule is moe_forward_band (ft_core.h:1617-1651). */
 #define GLMX_PATH_GEMV 0x100
@@ -97,8 +98,8 @@ GLMX_API int glmx_layer_set_act_limit(glmx_layer* layer, float limit);
 GLMX_API size_t glmx_workspace_bytes(const glmx_layer* layer, int ntok, int topk);
 
 /* Top-k token split: expert-major grouping of the picks into the workspace (offsets [E+1], rows sorted by
- * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward uses jobs of <= 4 rows on its decode paths,
- * <= 128 on the GEMM path). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
+ * (expert, token), pick -> row map, jobs of <= 8 rows; glmx_moe_forward uses jobs of <= 8 rows on its EXACT decode
+ * path, <= 4 in I16 mode, <= 128 on the GEMM path). Replaces ft_split (kernels/cpu_avx2/ft_tier_cu.cu:238-271,
  * kernels/k110/ft_split_fast.cu:200-235) and the job grouping of moe_forward (kernels/cpu_avx2/ft_core.h:1344-1349).
  * sel: device [ntok, topk] int32 or int64 (sel_dtype GLMX_I32 / GLMX_I64) of global expert ids; ids outside
  * [first_expert, first_expert + E) are skipped (negative ids mask a pick).

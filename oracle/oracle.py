@@ -342,11 +342,14 @@ def with_shared_routes(sel: np.ndarray, w: np.ndarray, E: int):
 # from the fp64 restatement, and one fp16 rounding step at the largest output (ulp16(max |out|) / RMS: the change a
 # single flip of an expert's fp16 down output makes there, which any fp32 accumulation order produces on some element
 # of a large enough input); rel-RMS within EXACT_SLACK x the reference kernels', with a floor of EXACT_RELRMS_FLOOR for
-# inputs where both happen to be almost exact. Averaged over many inputs the tests require the decode kernels to be at
-# least as close to the fp64 restatement as the band kernel, the more accurate of the two.
+# inputs where both happen to be almost exact: on a small layer (H=512, one token) a single fp16 rounding flip of one
+# intermediate value (a gate/up output, a down input) moves the whole output by up to ~2.3e-4 x RMS, and whether a
+# given fp32 accumulation order flips one there is chance; at BASELINE geometry the reference kernels themselves sit at
+# 2.3-3.7e-4, so there the bar is theirs. Averaged over many inputs the tests require the decode kernels to be at
+# least as close to the fp64 restatement as the band kernel, the more accurate of the two, in both metrics.
 EXACT_MAXABS = 2e-3
 EXACT_SLACK = 1.25
-EXACT_RELRMS_FLOOR = 5e-5
+EXACT_RELRMS_FLOOR = 2.5e-4
 
 
 def fp16_step(v: float) -> float:
