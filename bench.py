@@ -31,12 +31,11 @@ EXPERT_BYTES_K3 = 3 * (H // 16) * (I // 16) * 96          # 10,616,832 trellis b
 SCALE_BYTES = 3 * (H + I) * 2                              # suh + svh fp16 of gate, up, down: 46,080
 ROUTE_POOL = 16
 # DRAM bytes (read + write) per touched expert of one gate+up GEMV launch, from ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum). I16: a capture of this workload itself (B=64: 1829.98 MB read + 9.76 MB written over
-# 240.4 + 1 touched experts). EXACT: a smaller case (B=16: 414.9 MB + 4.0 MB over 57.5 experts; traffic grows with the
-# touched experts). roofline.traffic = this x the touched experts of the timed launches.
-GU_TRAFFIC_PER_EXPERT = {2: (1829.98e6 + 9.76e6) / 241.4, 1: (414.9e6 + 4.0e6) / 57.5}
+# dram__bytes_write.sum) on captures of this workload itself (B=64, 240.4 + 1 touched experts): I16 1829.98 MB read +
+# 9.76 MB written, EXACT 1729.75 MB + 7.89 MB. roofline.traffic = this x the touched experts of the timed launches.
+GU_TRAFFIC_PER_EXPERT = {2: (1829.98e6 + 9.76e6) / 241.4, 1: (1729.75e6 + 7.89e6) / 241.4}
 GU_TRAFFIC_SOURCE = {2: "bytes per launch (ncu, B=64 capture of this workload, per touched expert)",
-                     1: "bytes per launch (ncu, scaled from B=16)"}
+                     1: "bytes per launch (ncu, B=64 capture of this workload, per touched expert)"}
 
 
 def peaks():
@@ -684,8 +683,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=1, help="configs[3]: a stack of this many MoE layers per step (42 = the "
                     "full GLM-5.3 expert stack, about 129 GB at 1 GPU)")
-    ap.add_argument("--exchange", default="a2a", choices=["a2a", "allgather"], help="expert parallelism: per-destination "
-                    "all-to-all of the rows (a2a) or all-gather dispatch + reduce-scatter return")
+    ap.add_argument("--exchange", default="allgather", choices=["a2a", "allgather"], help="expert parallelism: all-gather "
+                    "dispatch + reduce-scatter return (no host synchronisation; the faster at decode sizes) or a "
+                    "per-destination all-to-all of the rows (a2a)")
     ap.add_argument("--peer", action="store_true", help="expert parallelism: return the partials with the combine's "
                     "peer-memory stores instead of NCCL's reduce-scatter")
     ap.add_argument("--sweep", default="1,8,32", help="extra decode batches measured (device time only)")

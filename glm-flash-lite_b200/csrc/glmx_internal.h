@@ -50,7 +50,8 @@ struct WsLayout
     // I16 mode
     size_t actb_gu, psum_gu, yraw_gu, actb_d, psum_d, isum_gu;
     size_t total;
-    int rows_max, jobs_max, jobs_max_i16, part_slots;
+    int rows_max, jobs_max, jobs_max_i16;
+    size_t part_bytes;        // EXACT split-K partial sums: [split][row][matrix][column] (hi, lo) pairs
 };
 
 WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas);

@@ -250,9 +250,17 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
         {
             // split-K: each piece stores its (hi, lo) pairs; the last to arrive adds them in split order (TwoSum on the
             // hi parts, lo parts added), so the split does not round the partial sums to fp32
-            constexpr int NV = NMAT * EXACT_MAXM * 128;
-            float2* part = a.partials + (size_t) item * NV;
-            for (int i = tid; i < NV; i += NCW * 32) __stcg(part + i, red[i]);
+            // the job's rows only, at [split][row][matrix][column]: entry v of its NMAT x job.z x 128 values is
+            // red[m][i][c]
+            const int ks = item - jn * S;
+            const int zr = job.z * 128, nvj = NMAT * zr;
+            const size_t kstride = (size_t) pl.R * NMAT * a.ndim;
+            auto slot = [&](int v) { const int m = v / zr, r = v - m * zr; return m * EXACT_MAXM * 128 + r; };
+            auto gidx = [&](int v) {
+                const int m = v / zr, r = v - m * zr, i = r >> 7, c = r & 127;
+                return ((size_t) (job.y + i) * NMAT + m) * a.ndim + nbi * 128 + c;
+            };
+            for (int v = tid; v < nvj; v += NCW * 32) __stcg(a.partials + ks * kstride + gidx(v), red[slot(v)]);
             __threadfence();
             consumer_sync();
             if (tid == 0)
@@ -263,17 +271,18 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
             consumer_sync();
             if (!s_last) continue;
             __threadfence();
-            const float2* p0 = a.partials + (size_t) jn * S * NV;
-            for (int i = tid; i < NV; i += NCW * 32)
+            for (int v = tid; v < nvj; v += NCW * 32)
             {
+                const int i = slot(v);
+                const float2* p0 = a.partials + gidx(v);
                 float h = 0.0f, l = 0.0f;
                 for (int k = 0; k < S; ++k)
                 {
-                    const float2 v = __ldcg(p0 + (size_t) k * NV + i);
-                    const float sum = __fadd_rn(h, v.x);
+                    const float2 pv = __ldcg(p0 + k * kstride);
+                    const float sum = __fadd_rn(h, pv.x);
                     const float bb = __fsub_rn(sum, h);
-                    const float e = __fadd_rn(__fsub_rn(h, __fsub_rn(sum, bb)), __fsub_rn(v.x, bb));
-                    l = __fadd_rn(__fadd_rn(l, v.y), e);
+                    const float e = __fadd_rn(__fsub_rn(h, __fsub_rn(sum, bb)), __fsub_rn(pv.x, bb));
+                    l = __fadd_rn(__fadd_rn(l, pv.y), e);
                     h = sum;
                 }
                 red[i] = make_float2(h, l);
@@ -579,7 +588,7 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     const int n = ntok * topk;
     const int rows = n + (L.has_shared ? ntok : 0);
     const int jobs = rows + 1;                       // each job holds >= 1 row
-    w.rows_max = rows; w.jobs_max = jobs; w.part_slots = 2 * grid_ctas;
+    w.rows_max = rows; w.jobs_max = jobs;
     size_t o = 0;
     auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + (bytes ? bytes : 1)); return at; };
     w.plan = take(sizeof(Plan));
@@ -598,7 +607,9 @@ WsLayout ws_layout(const Layer& L, int ntok, int topk, int grid_ctas)
     w.xu = take(sizeof(__half) * (size_t) rows * L.H);
     w.xd = take(sizeof(__half) * (size_t) rows * L.I);
     w.yrow = take(sizeof(float) * (size_t) rows * L.H);
-    w.partials = take(sizeof(float2) * (size_t) w.part_slots * 2 * EXACT_MAXM * 128);   // EXACT split-K (hi, lo) pairs
+    // EXACT split-K (hi, lo) pairs: room for as many splits as 2 x grid_ctas items of a full job would fill
+    w.part_bytes = sizeof(float2) * (size_t) 2 * grid_ctas * 2 * EXACT_MAXM * 128;
+    w.partials = take(w.part_bytes);
     // raw fp32 gate/up outputs (I16 GEMV: one slice; prefill GEMM: one slice per K split)
     w.yraw_gu = take(sizeof(float) * (size_t) PF_KSPLIT * rows * 2 * L.I);
     // I16 mode (decode-sized calls only): jobs of <= I16_MAXM rows of one expert: at most rows/4 + one partial job per

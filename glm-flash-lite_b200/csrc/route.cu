@@ -32,7 +32,8 @@ struct RouteArgs
     int maxm;                 // rows per job (EXACT GEMV 8, I16 4, GEMM 128)
     int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
     int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
-    int grid_ctas, part_slots;
+    int grid_ctas;
+    long long part_bytes;     // room for EXACT split-K partials: splits x rows x matrices x columns x 8 bytes
     Plan* plan;
     int* offsets; int* row_token; int* row_expert; int* row_pick; float* row_weight; int* pick_row; int4* jobs; int* row_job;
     int* cnt_gu; int* cnt_d; int* err;
@@ -88,18 +89,20 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total)
 // Split-K factor: the smallest divisor d of `stages` (each part >= 2 stages) with units * d >= target, never more
 // items than `slots` partial-sum slots.
 // K splits of a GEMV with `units` (job, column block) items of `stages` 128-input steps on `target` resident CTAs:
-// the divisor d of stages with the shortest critical path, ceil(units * d / target) waves of stages / d steps each
-// (the smaller d on ties, and units * d within the partial-sum slots)
-__device__ int pick_split(long long units, int stages, int target, int slots)
+// the divisor d of stages with the shortest critical path, ceil(units * d / target) waves of stages / d + ITEM_COST
+// steps each (an item's fixed cost - the split hand-off, the epilogue - measured at about two steps), the smaller d on
+// ties, and d within the room for partial sums, max_split
+constexpr int ITEM_COST = 2;
+__device__ int pick_split(long long units, int stages, int target, long long max_split)
 {
-    if (units <= 0 || units >= target) return 1;
+    if (units <= 0) return 1;
     int best = 1;
-    long long best_cost = stages;
+    long long best_cost = ((units + target - 1) / target) * (stages + ITEM_COST);
     for (int d = 2; d <= stages; ++d)
     {
         if (stages % d) continue;
-        if (units * d > slots) break;
-        const long long cost = ((units * d + target - 1) / target) * (stages / d);
+        if (d > max_split) break;
+        const long long cost = ((units * d + target - 1) / target) * (stages / d + ITEM_COST);
         if (cost < best_cost) { best_cost = cost; best = d; }
     }
     return best;
@@ -203,8 +206,10 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
     {
         Plan pl;
         pl.P = P; pl.R = P + nsh; pl.J = J;
-        pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_slots);
-        pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_slots);
+        // partial sums of split k: [k][row][matrix][column]: gate/up 2 x I columns per row, down H
+        const long long R = P + nsh > 0 ? P + nsh : 1;
+        pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_bytes / (R * 2 * 128 * a.nb_gu * 8));
+        pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_bytes / (R * 128 * a.nb_d * 8));
         pl.ntok = a.ntok; pl.topk = a.topk; pl.pad = 0;
         pl.next_gu = 0; pl.next_d = 0;
         *a.plan = pl;
@@ -223,7 +228,7 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
     a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared; a.first = L.first;
     a.nb_gu = L.I / 128; a.nb_d = L.H / 128; a.kq_gu = L.H / 128; a.kq_d = L.I / 128;
     a.grid_ctas = grid_ctas;
-    a.part_slots = lay.part_slots;
+    a.part_bytes = (long long) lay.part_bytes;
     a.plan = reinterpret_cast<Plan*>(ws + lay.plan);
     a.offsets = reinterpret_cast<int*>(ws + lay.offsets);
     a.row_token = reinterpret_cast<int*>(ws + lay.row_token);

@@ -4,7 +4,7 @@ Rank r of N holds routed experts [r*E/N, (r+1)*E/N) and a copy of the shared exp
 experts (the shard at local ids 0..n-1, the shared expert at local id n); every rank owns B tokens (the data-parallel
 part of the model gives each rank its own tokens). Two exchanges.
 
-exchange="a2a" (the default): per destination, only the tokens with a pick there travel.
+exchange="a2a": per destination, only the tokens with a pick there travel.
 
   shared     the shared expert on the rank's own rows, on a side stream, while the exchange below is in flight
   pack       glmx_ep_pack: per destination rank, its tokens (ascending), their rows and their picks in the
@@ -15,7 +15,7 @@ exchange="a2a" (the default): per destination, only the tokens with a pick there
   return     all-to-all of the fp32 results back to the token owners, in the order they were sent; glmx_ep_unpack_add
              adds each token's returned rows in rank order onto the shared expert's output
 
-exchange="allgather" (and "peer"):
+exchange="allgather" (the default; and "peer"):
 
   dispatch   all-gather of the ranks' token rows x [B, H] and their routing (sel, w) [B, k] -> [N*B, ...]
   split      global ids -> local ids of this shard (others' ids masked to -1), plus one extra pick per row: the
@@ -29,9 +29,12 @@ exchange="allgather" (and "peer"):
 
 With top-8 of 288 experts a token touches ≈ 5.3 of 8 shards, so gathering every token to every rank moves about as
 many bytes as a per-destination all-to-all, with static sizes: no host synchronisation for split sizes. The split is one
-kernel (glmx_ep_split). Measured on 8 B200s at global B=64 (one layer): 161.7 K tok/s with NCCL's reduce-scatter, 157.2
-K with the peer-memory return; NCCL reduces inside the NVSwitch (NVLS) and so moves half the bytes the point-to-point
-stores of the fused return do, which is why the reduce-scatter is the default. The reference has no expert-parallel mode
+kernel (glmx_ep_split). At decode sizes that wins: on 2 B200s at global B=64 the all-to-all's dispatch (count
+exchange, host synchronisation for NCCL's split sizes, rows and routing) takes 0.191 ms against the all-gather's 0.038
+ms, for rows of 12 KB each, so "allgather" is the default and "a2a" the form for batches whose rows, not latency,
+dominate. Measured on 8 B200s at global B=64 (one layer, an earlier build): 161.7 K tok/s with NCCL's reduce-scatter,
+157.2 K with the peer-memory return; NCCL reduces inside the NVSwitch (NVLS) and so moves half the bytes the
+point-to-point stores of the fused return do, which is why the reduce-scatter is the default return. The reference has no expert-parallel mode
 (its experts run on one host's CPU cores); this is the multi-GPU form of its MoE layer (configs[3] of the build's
 baseline: 288 experts over 2/4/8 GPUs).
 """
@@ -150,7 +153,7 @@ class ExpertParallelLayer:
     """
 
     def __init__(self, local, first: int, n: int, has_shared: bool = True, group=None, E: int | None = None,
-                 peer: bool = False, exchange: str = "a2a"):
+                 peer: bool = False, exchange: str = "allgather"):
         self.local = local
         self.first, self.n, self.has_shared = int(first), int(n), bool(has_shared)
         self.group = group
@@ -371,7 +374,7 @@ class ExpertParallelLayer:
 
 
 def from_bank(bank, group=None, device="cuda", act_limit: float = 0.0, peer: bool = False,
-              exchange: str = "a2a") -> ExpertParallelLayer:
+              exchange: str = "allgather") -> ExpertParallelLayer:
     """This rank's shard of a synth.ExpertBank (+ its shared expert), uploaded to `device`."""
     import numpy as np
 
