@@ -184,7 +184,7 @@ def run_reference_impl(args, rank, world):
 # ------------------------------------------------------------------------------------------------------------------
 def run_sweep(args, dev):
     """mixed-bitrate and skew sweep on one layer (288 routed + shared, H=6144, I=1536). Bitrates (gate, up,
-    down) = (2,2,2), (3,3,3), (4,4,4), (4,4,2); decode B = 1, 8, 64 (I16) and prefill T = 512, 2048 (EXACT, the
+    down) = (2,2,2), (3,3,3), (4,4,4), (4,4,2); decode B = 1, 8, 64 (--mode: EXACT by default) and prefill T = 512, 2048 (EXACT, the
     path chosen by the library: the tensor-core GEMM from 12 rows per expert) under uniform, Zipf(0.8 / 1.1 / 1.5) and
     hot-set (16 experts take 80 %) routing. Device time per call (CUDA
     events, warm, L2 not flushed between calls: every configuration streams more than L2 except B=1)."""
@@ -233,7 +233,7 @@ def run_sweep(args, dev):
                 sel = [torch.from_numpy(a).to(dev) for a, _ in rs]
                 wts = [torch.from_numpy(b).to(dev) for _, b in rs]
                 x = torch.randn((B, H), device=dev, generator=g).half()
-                ms = timed(layer, x, sel, wts, _lib.MODE_I16, 20, 3)
+                ms = timed(layer, x, sel, wts, args.mode, 20, 3)
                 touched = float(np.mean([np.unique(a).size + 1 for a, _ in rs]))
                 results.append({"bits": list(bits), "phase": "decode", "tokens": B, "routing": kind, "ms": ms,
                                 "tok_per_s": B / (ms / 1e3), "hbm_gbs": touched * expert_bytes / (ms / 1e3) / 1e9})
@@ -253,7 +253,8 @@ def run_sweep(args, dev):
                 and r["routing"] == "uniform")
     line = {"metric": "moe_layer_decode_tok_per_s", "value": head["tok_per_s"], "unit": "tok/s", "n_gpus": 1,
             "steps": 20, "warmup": 3, "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int16-act/int32-acc (decode), fp16/fp32-acc (prefill)", "data": "synthetic",
+            "vs_baseline": None, "data": "synthetic",
+            "dtype": ("int16-act/int32-acc" if args.mode == 2 else "fp16-weights/fp32-acc") + " (decode), fp16/fp32-acc (prefill)",
             "config": {"workload": "configs[4] mixed-bitrate and skew sweep (value: the K=3 uniform B=64 entry)",
                        "H": H, "I": I, "experts": E, "shared": 1, "topk": TOPK},
             "peak_hbm_gbs": pk["hbm_gbs"], "peak_kind": pk_kind, "results": results}
