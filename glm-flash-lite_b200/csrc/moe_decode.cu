@@ -4,8 +4,8 @@
 //   route   (route.cu)        picks -> expert-major rows, jobs of <= 8 rows
 //   prep                      per row: xt = fp16(had128(x * suh) * HAD) for gate and up   (ft_core.h:96-102)
 //   gemv<gate+up>             per (job, 128-col block, k-split): trellis tiles streamed by the tensor-copy engine into
-//                             a shared-memory ring, decoded in registers straight into mma.m16n8k16 A fragments (one
-//                             MMA per tile from zero, tile sums added in fp32, compensated per block); epilogue: out_block (ft_core.h:104-110) of g and u, a = fp16(silu(g) * u)
+//                             a shared-memory ring, decoded in registers straight into mma.m16n8k16 A fragments (chains
+//                             of 4 tile MMAs from zero, chain sums added in fp32, compensated per block); epilogue: out_block (ft_core.h:104-110) of g and u, a = fp16(silu(g) * u)
 //                             (ft_core.h:123-132, 980), then the down projection's input transform for that block
 //   gemv<down>                same main loop over the down matrix; epilogue out_block -> per-row fp32 y
 //   combine                   out[t] = sum over t's picks in pick order of w * y (+ shared expert), fp32
@@ -78,9 +78,7 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
 
-// m16n8k16 f16 x f16 -> f32 with C = 0: one 16-input tile of 16 outputs against 8 tokens. The MMA aligns its addends to
-// the largest and truncates below about 24 bits, so each MMA starts from zero (the error stays relative to one tile's
-// products, with no bias carried along the K loop) and the tile sums are added on the CUDA cores in fp32.
+// m16n8k16 f16 x f16 -> f32 with C = 0: one 16-input tile of 16 outputs against 8 tokens, the start of a chain
 __device__ __forceinline__ void hmma0(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
 {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
@@ -88,13 +86,29 @@ __device__ __forceinline__ void hmma0(float d[4], const uint32_t a[4], uint32_t 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
+// the same MMA accumulating onto d
+__device__ __forceinline__ void hmma_acc(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Tiles per accumulation chain inside the MMA. The MMA aligns its addends (the 16 products and C) to the largest and
+// drops the bits below about 24 bits of it, so a long chain, whose C outgrows the products, is shortened toward zero
+// step after step; chains of 4 tiles (64 inputs), added in fp32 and compensated per 128-input block, measured closer
+// to the fp64 restatement than single tiles (and than chains of 8, which are not).
+constexpr int TCHAIN = 4;
+static_assert(RB % TCHAIN == 0 && TCHAIN % 2 == 0, "chains of whole tile pairs within a stage");
+
 // One pipeline stage of one matrix, tensor-core form: lane (g, tq) of consumer warp w decodes its A fragments of tiles
 // (2rp, w) and (2rp + 1, w), loads token g's activations of both tiles (one 16-byte load: B fragments of the two MMAs)
-// and adds the two MMA results - outputs (g, g + 8) x tokens (2tq, 2tq + 1) - into its block sums.
+// and chains the two MMAs - outputs (g, g + 8) x tokens (2tq, 2tq + 1) - into the current TCHAIN-tile chain.
 template <int K>
 __device__ __forceinline__ void stage_tc(const uint8_t* st, int row_bytes, int t_off, int x_off, const LaneDecode<K>& L,
                                          const OnesFrag& ones, float blk[4])
 {
+    float ch[4];
 #pragma unroll
     for (int rp = 0; rp < RB / 2; ++rp)
     {
@@ -102,11 +116,13 @@ __device__ __forceinline__ void stage_tc(const uint8_t* st, int row_bytes, int t
         decode_frag_tc<K>(st + t_off + (2 * rp) * row_bytes, L, ones, a);
         decode_frag_tc<K>(st + t_off + (2 * rp + 1) * row_bytes, L, ones, b);
         const uint4 xv = *reinterpret_cast<const uint4*>(st + x_off + rp * 64);
-        float d[4], e[4];
-        hmma0(d, a, xv.x, xv.y);
-        hmma0(e, b, xv.z, xv.w);
+        // chains of TCHAIN tiles inside the MMA accumulator (the first from zero), each added to the block sum in fp32
+        if ((2 * rp) % TCHAIN == 0) hmma0(ch, a, xv.x, xv.y);
+        else hmma_acc(ch, a, xv.x, xv.y);
+        hmma_acc(ch, b, xv.z, xv.w);
+        if ((2 * rp + 2) % TCHAIN == 0)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) blk[c] = __fadd_rn(__fadd_rn(blk[c], d[c]), e[c]);
+            for (int c = 0; c < 4; ++c) blk[c] = __fadd_rn(blk[c], ch[c]);
     }
 }
 
@@ -153,8 +169,8 @@ __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, u
 // EXACT-mode GEMV (one persistent kernel per phase). Items (job of <= 8 rows, 128-column block, K split); per item the
 // producer warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per
 // row), the 8 consumer warps decode (byte sums on the integer tensor pipe, codebook by HFMA2) and form each 16x16 tile's
-// products with one m16n8k16 MMA against the job's 8 token columns, started from zero (stage_tc); the tile sums are
-// added on the CUDA cores, block sums compensated (Fast2Sum, TwoSum across K splits).
+// products with m16n8k16 MMAs against the job's 8 token columns in chains of TCHAIN tiles started from zero
+// (stage_tc); the chain sums are added on the CUDA cores, block sums compensated (Fast2Sum, TwoSum across K splits).
 template <int K0, int K1, int NMAT, bool GATEUP>
 __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 {
