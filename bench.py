@@ -110,6 +110,15 @@ def unique_touched(routes):
     return [int(np.unique(s).size) for s, _ in routes]
 
 
+def decode_config(B, mode, world, uniq_mean):
+    """The config dict of the configs[1] decode line, shared by both arms (the reference arm reports the same one)."""
+    return {"workload": f"configs[1] decode MoE layer B={B} (288 routed + 1 shared, H=6144, I=1536, K=3, top-8)",
+            "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": {1: "EXACT", 2: "I16"}[mode],
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (touched trellis per step > 126 MB)" if B >= 32 else "L2 flushed between steps",
+            "unique_experts_per_step": uniq_mean}
+
+
 # ------------------------------------------------------------------------------------------------------------------
 def cpu_reference_run(B: int, seconds: float, threads: int, seed: int = 0):
     """The reference's moe_forward (EXACT mode, ft_core.h:1338-1407) at BASELINE geometry on the host cores, with
@@ -158,7 +167,9 @@ def run_reference_impl(args, rank, world):
     layer = ref.layer(bank, with_shared=True)
     cpus = sorted(os.sched_getaffinity(0))
     ref.start_pool(threads, cpus[:threads])
-    routes = [O.with_shared_routes(s, w, E) for s, w in make_routes(args.batch, 1000)]
+    raw = make_routes(args.batch, 1000)                       # the GPU arm's rank-0 routes
+    uq = unique_touched(raw)
+    routes = [O.with_shared_routes(s, w, E) for s, w in raw]
     x = synth.make_x(args.batch, H, 7).astype(np.float32)
     for i in range(args.warmup):
         ref.moe_forward(layer, x, *routes[i % len(routes)], mode=1)
@@ -172,9 +183,8 @@ def run_reference_impl(args, rank, world):
     print(json.dumps({
         "impl": "reference", "metric": "moe_layer_decode_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32-acc/fp16-weights", "data": "synthetic",
-        "config": {"workload": f"configs[1] decode MoE layer B={args.batch}", "H": H, "I": I, "experts": E, "shared": 1,
-                   "bits": 3, "topk": TOPK, "batch": args.batch, "mode": "EXACT"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16-weights/fp32-acc", "data": "synthetic",
+        "config": decode_config(args.batch, 1, world, statistics.mean(uq)),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
                          "sample": f"{args.steps} full B={args.batch} layer calls of ft_core.h moe_forward (EXACT)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -907,11 +917,7 @@ def main():
         "metric": "moe_layer_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": T_ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": {1: "fp16-weights/fp32-acc", 2: "int16-act/int32-acc"}[args.mode], "data": "synthetic",
-        "config": {"workload": f"configs[1] decode MoE layer B={B} (288 routed + 1 shared, H=6144, I=1536, K=3, top-8)",
-                   "batch": B, "H": H, "I": I, "experts": E, "shared": 1, "bits": 3, "topk": TOPK, "mode": {1: "EXACT", 2: "I16"}[args.mode],
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (touched trellis per step > 126 MB)" if B >= 32 else "L2 flushed between steps",
-                   "unique_experts_per_step": statistics.mean(r["uniq"])},
+        "config": decode_config(B, args.mode, world, statistics.mean(r["uniq"])),
         "hbm_gbs_layer": achieved_layer_gbs,
         "roofline": {"bound": "hbm", "kernel": "gemv<gate+up>", "achieved": gu_gbs, "peak": peak, "unit": "GB/s",
                      "frac": gu_gbs / peak, "peak_kind": pk_kind,
