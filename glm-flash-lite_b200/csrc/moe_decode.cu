@@ -362,8 +362,9 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 }
 
 // ---- prep: xt = fp16(had128(x * suh) * HAD) per row and projection (gate, up) ----
-// One warp per (token, 128-input block, projection): the token's x block is loaded once and transformed for every row
-// of the token (its routed picks, then the shared expert's row), each with that row's expert's suh.
+// One warp per (token, 128-input block, projection) and row group: the token's x block is loaded once per warp and
+// transformed for the token's rows of its group (its routed picks, then the shared expert's row), each with that row's
+// expert's suh. Small batches give every row its own warp (groups = rows per token); large ones one warp per block.
 struct PrepArgs
 {
     const Plan* plan;
@@ -373,6 +374,7 @@ struct PrepArgs
     const __half* suh_g; const __half* suh_u;
     __half* xg; __half* xu;
     int natural;          // 1: natural input order (tensor-core GEMM), 0: PERM16 order inside 16-row tiles (GEMV)
+    int groups;           // warps per (token, block, projection): warp g transforms the token's rows g, g + groups, ...
 };
 
 __device__ __forceinline__ float load_x(const void* x, int dt, size_t i)
@@ -388,16 +390,17 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a)
     const int nbk = a.H / 128;
     const long long wid = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const int t = (int) (wid / (2 * nbk));
+    const int t = (int) (wid / (2 * nbk * a.groups));
     if (t >= a.ntok) return;
-    const int rem = (int) (wid % (2 * nbk)), p = rem / nbk, b = rem % nbk;
+    const int rem = (int) (wid % (2 * nbk * a.groups)), grp = rem % a.groups, pb = rem / a.groups;
+    const int p = pb / nbk, b = pb % nbk;
     float xv[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) xv[q] = load_x(a.x, a.x_dtype, (size_t) t * a.H + b * 128 + lane + 32 * q);
     const __half* suh_p = p ? a.suh_u : a.suh_g;
     __half* out_p = p ? a.xu : a.xg;
     const int nk = a.topk + (a.has_shared ? 1 : 0);
-    for (int k = 0; k < nk; ++k)
+    for (int k = grp; k < nk; k += a.groups)
     {
         int r, e;
         if (k < a.topk)
@@ -657,7 +660,10 @@ cudaError_t launch_prep_exact(const Layer& L, const void* x, int x_dtype, int nt
     p.xg = reinterpret_cast<__half*>(ws + lay.xg);
     p.xu = reinterpret_cast<__half*>(ws + lay.xu);
     p.natural = natural ? 1 : 0;
-    const long long warps = (long long) ntok * 2 * (L.H / 128);
+    // small batches: one warp per row of a token block (the token's rows in parallel); large ones: one warp per token
+    // block serving all its rows (the block loaded once)
+    p.groups = ntok <= 16 ? topk + (L.has_shared ? 1 : 0) : 1;
+    const long long warps = (long long) ntok * 2 * (L.H / 128) * p.groups;
     return launch_chained(prep_kernel, dim3((unsigned) ((warps + 7) / 8)), dim3(256), 0, st, p);
 }
 

@@ -193,3 +193,34 @@ def test_layer_from_exllamav3_tables(monkeypatch):
             assert int(seen["ptrs"][e, p]) == inner.trellis.data_ptr()
             assert torch.equal(seen["suh"][p][e], inner.suh) and torch.equal(seen["svh"][p][e], inner.svh)
     assert len(seen["keep"]) == 15
+
+
+# ---- glmx.hc: the reference's apply_partials / finalize_norm mirror, argument checks (CPU tensors, no launch) ----------
+
+def test_hc_mirror_argument_checks():
+    from glmx import hc
+    R, D = 2, 256
+    x = torch.zeros(R, 4, D)
+    fn = torch.zeros(24, 4 * D, dtype=torch.float16)
+    part = torch.zeros(R, 4 * D // 128, 25)
+    hc.check_mix_args(x, fn, part)                                  # well-formed: no error
+    with pytest.raises(ValueError, match="x must be"):
+        hc.check_mix_args(torch.zeros(R, 3, D), fn, part)
+    with pytest.raises(ValueError, match="D % 128"):
+        hc.check_mix_args(torch.zeros(R, 4, 200), fn, part)
+    with pytest.raises(ValueError, match="fn must be"):
+        hc.check_mix_args(x, fn.float(), part)
+    with pytest.raises(ValueError, match="fn must be"):
+        hc.check_mix_args(x, torch.zeros(24, 2 * D, dtype=torch.float16), part)
+    with pytest.raises(ValueError, match="partials must be"):
+        hc.check_mix_args(x, fn, torch.zeros(R, 4 * D // 128, 24))
+    with pytest.raises(ValueError, match="y must be"):
+        hc.apply_partials(x, torch.zeros(R, D, dtype=torch.bfloat16), torch.zeros(R, 4), torch.zeros(R, 4, 4), fn, part)
+    with pytest.raises(ValueError, match="needs post and comb"):
+        hc.apply_partials(x, torch.zeros(R, D), None, None, fn, part)
+    with pytest.raises(ValueError, match="nw must be"):
+        hc.finalize_norm(x, part, torch.zeros(24), torch.zeros(3), torch.zeros(R, 4), torch.zeros(R, 4, 4),
+                         torch.zeros(D), torch.zeros(R, D, dtype=torch.float16), 1e-6, 1e-6, 20, 1e-5, 0.0, 1.0)
+    with pytest.raises(ValueError, match="out must be"):
+        hc.finalize_norm(x, part, torch.zeros(24), torch.zeros(3), torch.zeros(R, 4), torch.zeros(R, 4, 4),
+                         torch.zeros(D, dtype=torch.float16), torch.zeros(R, D), 1e-6, 1e-6, 20, 1e-5, 0.0, 1.0)
