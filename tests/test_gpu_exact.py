@@ -103,16 +103,17 @@ def _bench_inputs(seed, B=64):
     return x, sel, w
 
 
-@pytest.mark.parametrize("mode", [1, 2])
-def test_bench_config_parity(oracle, dev, big_layer, mode):
-    """B=64 over 288 routed experts + shared (the bench's own workload), the whole batch on the GPU, 16 seeded rows
-    checked on the CPU: EXACT by the EXACT rule, I16 bit for bit against the restatement of the reference's I16 kernel."""
+@pytest.mark.parametrize("mode,B", [(1, 64), (2, 64), (1, 8), (1, 16)])
+def test_bench_config_parity(oracle, dev, big_layer, mode, B):
+    """B=64 over 288 routed experts + shared (the bench's own workload; B=8 and 16 also split K across CTAs), the whole
+    batch on the GPU, up to 16 seeded rows checked on the CPU: EXACT by the EXACT rule, I16 bit for bit against the
+    restatement of the reference's I16 kernel."""
     layer = big_layer[0]
-    x, sel, w = _bench_inputs(7001)
+    x, sel, w = _bench_inputs(7001 + B, B)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     got = layer.forward(t(x), t(sel), t(w), mode=mode).cpu().numpy()
-    assert layer.check_device(64, 8) == 0
-    rows = np.sort(np.random.default_rng(7002).choice(64, 16, replace=False))
+    assert layer.check_device(B, 8) == 0
+    rows = np.sort(np.random.default_rng(7002).choice(B, min(B, 16), replace=False))
     touched = np.unique(sel[rows])
     remap = {int(e): i for i, e in enumerate(touched)}
     bank = _host_bank(big_layer, touched)
@@ -122,7 +123,7 @@ def test_bench_config_parity(oracle, dev, big_layer, mode):
     if mode == 2:
         np.testing.assert_array_equal(got[rows], want)
     else:
-        assert_exact_mode(got[rows], want, *reference_outputs(bank, xs, ss, ws), label="configs[1] B=64 E=288")
+        assert_exact_mode(got[rows], want, *reference_outputs(bank, xs, ss, ws), label=f"configs[1] B={B} E=288")
 
 
 @pytest.mark.parametrize("mode", [1, 2])
