@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
     const int E = a.E;
     int* cnt = sm;                                   // [E]
     int* base = cnt + E;                             // [E]
-    unsigned short* wcnt = reinterpret_cast<unsigned short*>(base + E);   // [32][E]
+    int* jbase = base + E;                           // [E] first job of each expert
+    unsigned short* wcnt = reinterpret_cast<unsigned short*>(jbase + E);  // [32][E]
     __shared__ int warp_sums[32];
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int n = a.ntok * a.topk;
@@ -142,11 +143,12 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
     {
         a.offsets[tid] = off;
         base[tid] = off;
+        cnt[tid] = off;                              // from here on cnt holds the expert's first row
+        jbase[tid] = joff;
         for (int q = 0; q < nj; ++q)
         {
             const int r0 = off + q * maxm, m = min(maxm, c - q * maxm);
             a.jobs[joff + q] = make_int4(tid, r0, m, 0);
-            for (int i = 0; i < m; ++i) a.row_job[r0 + i] = joff + q;
         }
     }
     if (tid == 0) a.offsets[E] = P;
@@ -156,11 +158,11 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
     {
         const int r0 = P + q * maxm, m = min(maxm, nsh - q * maxm);
         a.jobs[Jr + q] = make_int4(E, r0, m, 0);
-        for (int i = 0; i < m; ++i) a.row_job[r0 + i] = Jr + q;
     }
     for (int t = tid; t < nsh; t += RT)
     {
         a.row_token[P + t] = t; a.row_expert[P + t] = E; a.row_pick[P + t] = -1; a.row_weight[P + t] = 1.0f;
+        a.row_job[P + t] = Jr + t / maxm;
     }
     __syncthreads();
 
@@ -187,6 +189,7 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
             for (int w2 = 0; w2 < wid; ++w2) pre += wcnt[w2 * E + e];
             const int r = base[e] + pre + lrank;
             a.row_token[r] = p / a.topk; a.row_expert[r] = e; a.row_pick[r] = p; a.row_weight[r] = wt;
+            a.row_job[r] = jbase[e] + (r - cnt[e]) / maxm;
             a.pick_row[p] = r;
         }
         __syncthreads();
@@ -241,7 +244,7 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
     a.cnt_gu = reinterpret_cast<int*>(ws + lay.cnt_gu);
     a.cnt_d = reinterpret_cast<int*>(ws + lay.cnt_d);
     a.err = reinterpret_cast<int*>(ws + lay.err);
-    const size_t smem = sizeof(int) * 2 * L.E + sizeof(unsigned short) * 32 * L.E + 16;
+    const size_t smem = sizeof(int) * 3 * L.E + sizeof(unsigned short) * 32 * L.E + 16;
     static bool attr_set[64] = {};
     if (L.device < 0 || L.device >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[L.device])
