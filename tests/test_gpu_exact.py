@@ -4,9 +4,10 @@ determinism of the decode kernels (work taken from counters, split-K finished by
 
 The EXACT rule (oracle.exact_bars, the same as the smoke check), on each input: max-abs within the largest of 2e-3,
 1.25 x the distance of the reference's own EXACT kernels - moe_forward and its band schedule moe_forward_band - from the
-fp64 restatement, and one fp16 step at the largest output (a single rounding flip there); rel-RMS within 1.25 x the
-reference kernels'; over all seeded decode inputs together the GPU must be at least as close to the fp64 restatement
-as the band kernel (the more accurate of the two), in both metrics."""
+fp64 restatement, and one fp16 step at the largest output (a single rounding flip there); rel-RMS within the larger of
+1.25 x the reference kernels' and 2.5e-4 (one rounding flip of an intermediate value on a small layer); over all
+seeded decode inputs together the GPU must be at least as close to the fp64 restatement as the band kernel (the more
+accurate of the two), in both metrics."""
 import numpy as np
 import pytest
 
