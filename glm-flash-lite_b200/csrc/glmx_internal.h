@@ -105,6 +105,11 @@ cudaError_t launch_chained(void (*kernel)(P...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
 }
 
+// 128-input blocks per pipeline stage of the EXACT GEMV of projection proj (0: gate/up over H, 2: down over I): 2 where
+// the matrices' bitrates are at most 3 and K is a multiple of 256 (a stage of two blocks fits the ring three times),
+// else 1. The split plan counts K splits in these stages.
+int exact_stage_blocks(const Layer& L, int proj);
+
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const void* w, int w_dtype, int ntok, int topk,
                          int maxm, uint8_t* ws, const WsLayout& lay, int grid_ctas, cudaStream_t st);

@@ -26,27 +26,29 @@ namespace glmx {
 
 namespace {
 
-constexpr int RB = 8;        // k-rows (16 inputs each) per pipeline stage = one 128-input block
+constexpr int RB = 8;        // k-rows (16 inputs each) per 128-input block
 constexpr int NCW = 8;       // consumer warps = n-tiles per 128-output block
 constexpr int NTHR = (NCW + 1) * 32;
-constexpr int XROW = 256;    // bytes per staged activation row: one 128-input block, fp16, in the lane order of gemv_xpos
-// stride of the staged activation rows in a stage: lane (g, tq) reads row g, and a 320-byte stride puts the two rows
-// of each quarter-warp's 16-byte loads in different bank halves
-constexpr int XSTR = 320;
+constexpr int XBLK = 256;    // bytes of one staged activation row per 128-input block (fp16, lane order of gemv_xpos)
 #ifndef GLMX_EXACT_CTAS
 #define GLMX_EXACT_CTAS 3
 #endif
 constexpr int CTAS_PER_SM = GLMX_EXACT_CTAS;
 constexpr int RING_BYTES = (CTAS_PER_SM >= 3 ? 56 : 88) * 1024;    // per CTA; CTAS_PER_SM rings share an SM
 
-// One pipeline stage holds RB k-tile rows x 8 tiles of ONE matrix (an item of the gate/up kernel runs all stages of
-// gate, then all stages of up) and the job's activation rows for that block.
-template <int K0, int K1, int NMAT>
+// One pipeline stage holds HB 128-input blocks (HB * RB k-tile rows x 8 tiles) of ONE matrix (an item of the gate/up
+// kernel runs all stages of gate, then all stages of up) and the job's activation rows for them. Two blocks per stage
+// halve the per-stage costs (the ring's waits and arrivals, the addressing); the block sums stay per 128 inputs.
+template <int K0, int K1, int NMAT, int HB>
 struct Cfg
 {
     static constexpr int TB0 = 32 * K0, TB1 = 32 * K1;
     static constexpr int ROW0 = 8 * TB0, ROW1 = 8 * TB1;
-    static constexpr int MAT = RB * (ROW0 > ROW1 ? ROW0 : ROW1);
+    static constexpr int MAT = HB * RB * (ROW0 > ROW1 ? ROW0 : ROW1);
+    static constexpr int XROW = HB * XBLK;   // bytes per staged activation row
+    // stride of the staged activation rows: lane (g, tq) reads row g, and a stride of 64 mod 128 bytes puts the two
+    // rows of each quarter-warp's 16-byte loads in different bank halves
+    static constexpr int XSTR = XROW + 64;
     static constexpr int XS = EXACT_MAXM * XSTR;
     static constexpr int STAGE = (MAT + XS + 127) / 128 * 128;   // tensor copies land 128-byte aligned
     static constexpr int NST = RING_BYTES / STAGE < 3 ? 3 : (RING_BYTES / STAGE > 12 ? 12 : RING_BYTES / STAGE);
@@ -54,6 +56,7 @@ struct Cfg
     static constexpr int SMEM = NST * STAGE + RED + 2 * NST * 8;
     static_assert(STAGE % 128 == 0 && MAT % 128 == 0, "stage alignment");
     static_assert(EXACT_MAXM == 8, "EXACT GEMV jobs of up to 8 rows: the 8 token columns of one MMA");
+    static_assert(HB == 1 || HB == 2, "one or two 128-input blocks per stage");
 };
 
 struct GemvArgs
@@ -99,7 +102,7 @@ __device__ __forceinline__ void hmma_acc(float d[4], const uint32_t a[4], uint32
 // step after step; chains of 4 tiles (64 inputs), added in fp32 and compensated per 128-input block, measured closer
 // to the fp64 restatement than single tiles (and than chains of 8, which are not).
 constexpr int TCHAIN = 4;
-static_assert(RB % TCHAIN == 0 && TCHAIN % 2 == 0, "chains of whole tile pairs within a stage");
+static_assert(RB % TCHAIN == 0 && TCHAIN % 2 == 0, "chains of whole tile pairs within a block");
 
 // One pipeline stage of one matrix, tensor-core form: lane (g, tq) of consumer warp w decodes its A fragments of tiles
 // (2rp, w) and (2rp + 1, w), loads token g's activations of both tiles (one 16-byte load: B fragments of the two MMAs)
@@ -128,14 +131,14 @@ __device__ __forceinline__ void stage_tc(const uint8_t* st, int row_bytes, int t
 
 // The k-stages of one item, tensor-core form (any job of <= 8 rows): per lane 4 (output, token) block sums, each fed
 // once per 128-input block into a (hi, lo) pair by Fast2Sum; the pairs go to red[mat][token][col].
-template <int K0, int K1, int NMAT>
+template <int K0, int K1, int NMAT, int HB>
 __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, uint64_t* empty, float2* red, int kqs,
                                                 int& s, uint32_t& ph, volatile int* s_abort, int* err, int warp, int lane,
                                                 const LaneDecode<K0>& L0, const LaneDecode<K1>& L1, const OnesFrag& ones)
 {
-    using C = Cfg<K0, K1, NMAT>;
+    using C = Cfg<K0, K1, NMAT, HB>;
     const int g = lane >> 2, tq = lane & 3;
-    const int x_off = C::MAT + g * XSTR + tq * 16;
+    const int x_off = C::MAT + g * C::XSTR + tq * 16;
 #pragma unroll 1
     for (int m = 0; m < NMAT; ++m)
     {
@@ -145,19 +148,26 @@ __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, u
         {
             if (!*s_abort && !mbar_wait_bounded(&full[s], ph)) { atomicOr(err, ERR_TIMEOUT_FULL); *s_abort = 1; }
             const uint8_t* st = ring + s * C::STAGE;
-            float blk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (NMAT == 1 || m == 0) stage_tc<K0>(st, C::ROW0, warp * C::TB0, x_off, L0, ones, blk);
-            else stage_tc<K1>(st, C::ROW1, warp * C::TB1, x_off, L1, ones, blk);
+#pragma unroll 1
+            for (int hb = 0; hb < HB; ++hb)
+            {
+                // block hb: its tiles RB * hb k-rows in, its activations XBLK * hb bytes into each staged row
+                float blk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (NMAT == 1 || m == 0)
+                    stage_tc<K0>(st + hb * RB * C::ROW0, C::ROW0, warp * C::TB0, x_off + hb * (XBLK - RB * C::ROW0), L0, ones, blk);
+                else
+                    stage_tc<K1>(st + hb * RB * C::ROW1, C::ROW1, warp * C::TB1, x_off + hb * (XBLK - RB * C::ROW1), L1, ones, blk);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                {
+                    const float sum = __fadd_rn(hi[c], blk[c]);
+                    lo[c] = __fadd_rn(lo[c], __fsub_rn(blk[c], __fsub_rn(sum, hi[c])));
+                    hi[c] = sum;
+                }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (++s == C::NST) { s = 0; ph ^= 1u; }
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-            {
-                const float sum = __fadd_rn(hi[c], blk[c]);
-                lo[c] = __fadd_rn(lo[c], __fsub_rn(blk[c], __fsub_rn(sum, hi[c])));
-                hi[c] = sum;
-            }
         }
         float2* rm = red + m * EXACT_MAXM * 128;
         const int o = warp * 16 + g;
@@ -171,10 +181,10 @@ __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, u
 // row), the 8 consumer warps decode (byte sums on the integer tensor pipe, codebook by HFMA2) and form each 16x16 tile's
 // products with m16n8k16 MMAs against the job's 8 token columns in chains of TCHAIN tiles started from zero
 // (stage_tc); the chain sums are added on the CUDA cores, block sums compensated (Fast2Sum, TwoSum across K splits).
-template <int K0, int K1, int NMAT, bool GATEUP>
+template <int K0, int K1, int NMAT, bool GATEUP, int HB>
 __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
 {
-    using C = Cfg<K0, K1, NMAT>;
+    using C = Cfg<K0, K1, NMAT, HB>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;
     float2* red = reinterpret_cast<float2*>(smem + C::NST * C::STAGE);
@@ -196,7 +206,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
     const Plan pl = *a.plan;
     const int nb = a.ntn / 8;
     const int S = GATEUP ? pl.S_gu : pl.S_d;
-    const int kqs = (a.kt / RB) / S;                        // stages per item and matrix
+    const int kqs = (a.kt / (HB * RB)) / S;                 // stages per item and matrix
     const int items = pl.J * nb * S;                        // < 2^31: J <= rows + 1, nb <= 64, S <= 64
 
     if (warp == NCW)
@@ -216,18 +226,20 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
                 const CUtensorMap* map = a.tmaps + job.x * 3 + a.proj0 + m;
                 const int tb = m ? C::TB1 : C::TB0, rowb = m ? C::ROW1 : C::ROW0;
                 const __half* xin = m ? a.xin1 : a.xin0;
-                const uint32_t bytes = (uint32_t) (RB * rowb + job.z * XROW);
+                const uint32_t bytes = (uint32_t) (HB * RB * rowb + job.z * C::XROW);
                 for (int q = 0; q < kqs; ++q)
                 {
                     if (!s_abort && !mbar_wait_bounded(&empty[s], ph ^ 1u)) { atomicOr(a.err, ERR_TIMEOUT_EMPTY); s_abort = 1; }
                     if (s_abort) break;
-                    const int kr = (ks * kqs + q) * RB;
+                    const int kr = (ks * kqs + q) * HB * RB;
                     uint8_t* st = ring + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], bytes);
-                    // the stage's RB k-tile rows x 8 tiles of the matrix: one tensor copy (x in 32-bit words)
-                    tma_load_2d(st, map, nbi * 8 * tb / 4, kr, &full[s]);
+                    // the stage's HB x RB k-tile rows x 8 tiles of the matrix: one tensor copy (x in 32-bit words) per
+                    // block of RB rows
+                    for (int hb = 0; hb < HB; ++hb)
+                        tma_load_2d(st + hb * RB * rowb, map, nbi * 8 * tb / 4, kr + hb * RB, &full[s]);
                     for (int i = 0; i < job.z; ++i)
-                        bulk_g2s(st + C::MAT + i * XSTR, xin + (size_t) (job.y + i) * a.kdim + kr * 16, XROW, &full[s]);
+                        bulk_g2s(st + C::MAT + i * C::XSTR, xin + (size_t) (job.y + i) * a.kdim + kr * 16, C::XROW, &full[s]);
                     ++issued;
                     if (++s == C::NST) { s = 0; ph ^= 1u; }
                 }
@@ -260,7 +272,7 @@ __global__ void __maxnreg__(CTAS_PER_SM >= 3 ? 72 : 112) gemv_kernel(GemvArgs a)
         const int jn = item / S;
         const int nbi = jn % nb, j = jn / nb;
         const int4 job = a.jobs[j];
-        item_consume_tc<K0, K1, NMAT>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones);
+        item_consume_tc<K0, K1, NMAT, HB>(ring, full, empty, red, kqs, s, ph, &s_abort, a.err, warp, lane, L0, L1, ones);
         consumer_sync();
         if (S > 1)
         {
@@ -535,18 +547,27 @@ __global__ void decode_tiles_kernel(const uint8_t* tiles, int ntiles, uint16_t* 
     o[(r0 + 8) * 16 + g + 8] = a[3] & 0xffff;   o[(r1 + 8) * 16 + g + 8] = a[3] >> 16;
 }
 
-template <int K0, int K1, int NMAT, bool GATEUP>
-cudaError_t launch_gemv(const Layer& L, const GemvArgs& a, int grid, cudaStream_t st)
+template <int K0, int K1, int NMAT, bool GATEUP, int HB>
+cudaError_t launch_gemv_hb(const Layer& L, const GemvArgs& a, int grid, cudaStream_t st)
 {
-    using C = Cfg<K0, K1, NMAT>;
+    using C = Cfg<K0, K1, NMAT, HB>;
     static bool attr_set[64] = {};
     if (!attr_set[L.device])
     {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<K0, K1, NMAT, GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<K0, K1, NMAT, GATEUP, HB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set[L.device] = true;
     }
-    return launch_chained(gemv_kernel<K0, K1, NMAT, GATEUP>, dim3(grid), dim3(NTHR), C::SMEM, st, a);
+    return launch_chained(gemv_kernel<K0, K1, NMAT, GATEUP, HB>, dim3(grid), dim3(NTHR), C::SMEM, st, a);
+}
+
+// the stage form the split plan was made for (exact_stage_blocks); two-block stages exist for bitrates up to 3 only
+template <int K0, int K1, int NMAT, bool GATEUP>
+cudaError_t launch_gemv(const Layer& L, const GemvArgs& a, int grid, cudaStream_t st)
+{
+    if constexpr (K0 <= 3 && K1 <= 3)
+        if (exact_stage_blocks(L, GATEUP ? 0 : 2) == 2) return launch_gemv_hb<K0, K1, NMAT, GATEUP, 2>(L, a, grid, st);
+    return launch_gemv_hb<K0, K1, NMAT, GATEUP, 1>(L, a, grid, st);
 }
 
 template <int K0>
@@ -583,6 +604,13 @@ cudaError_t launch_down(const Layer& L, const GemvArgs& a, int grid, cudaStream_
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
+
+int exact_stage_blocks(const Layer& L, int proj)
+{
+    const int kdim = proj == 0 ? L.H : L.I;
+    const bool low = proj == 0 ? (L.bits[0] <= 3 && L.bits[1] <= 3) : L.bits[2] <= 3;
+    return low && kdim % 256 == 0 ? 2 : 1;
+}
 
 int gemv_sm_count(const Layer& L)
 {

@@ -31,7 +31,8 @@ struct RouteArgs
     int first;                // global id of local expert 0
     int maxm;                 // rows per job (EXACT GEMV 8, I16 4, GEMM 128)
     int nb_gu, nb_d;          // n-blocks of 128 of the gate/up and down kernels
-    int kq_gu, kq_d;          // RB-stages per full K of gate/up and down (K / 128)
+    int kq_gu, kq_d;          // GEMV pipeline stages per full K of gate/up and down
+    int cost_gu, cost_d;      // an item's fixed cost in those stages
     int grid_ctas;
     long long part_bytes;     // room for EXACT split-K partials: splits x rows x matrices x columns x 8 bytes
     Plan* plan;
@@ -86,23 +87,20 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total)
     return before;
 }
 
-// Split-K factor: the smallest divisor d of `stages` (each part >= 2 stages) with units * d >= target, never more
-// items than `slots` partial-sum slots.
-// K splits of a GEMV with `units` (job, column block) items of `stages` 128-input steps on `target` resident CTAs:
-// the divisor d of stages with the shortest critical path, ceil(units * d / target) waves of stages / d + ITEM_COST
-// steps each (an item's fixed cost - the split hand-off, the epilogue - measured at about two steps), the smaller d on
-// ties, and d within the room for partial sums, max_split
-constexpr int ITEM_COST = 2;
-__device__ int pick_split(long long units, int stages, int target, long long max_split)
+// K splits of a GEMV with `units` (job, column block) items of `stages` pipeline stages on `target` resident CTAs:
+// the divisor d of stages with the shortest critical path, ceil(units * d / target) waves of stages / d + item_cost
+// stages each (an item's fixed cost - the split hand-off, the epilogue - measured at about two 128-input steps), the
+// smaller d on ties, and d within the room for partial sums, max_split
+__device__ int pick_split(long long units, int stages, int target, long long max_split, int item_cost)
 {
     if (units <= 0) return 1;
     int best = 1;
-    long long best_cost = ((units + target - 1) / target) * (stages + ITEM_COST);
+    long long best_cost = ((units + target - 1) / target) * (stages + item_cost);
     for (int d = 2; d <= stages; ++d)
     {
         if (stages % d) continue;
         if (d > max_split) break;
-        const long long cost = ((units * d + target - 1) / target) * (stages / d + ITEM_COST);
+        const long long cost = ((units * d + target - 1) / target) * (stages / d + item_cost);
         if (cost < best_cost) { best_cost = cost; best = d; }
     }
     return best;
@@ -211,8 +209,8 @@ __global__ void __launch_bounds__(RT) route_kernel(RouteArgs a)
         pl.P = P; pl.R = P + nsh; pl.J = J;
         // partial sums of split k: [k][row][matrix][column]: gate/up 2 x I columns per row, down H
         const long long R = P + nsh > 0 ? P + nsh : 1;
-        pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_bytes / (R * 2 * 128 * a.nb_gu * 8));
-        pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_bytes / (R * 128 * a.nb_d * 8));
+        pl.S_gu = pick_split((long long) J * a.nb_gu, a.kq_gu, a.grid_ctas, a.part_bytes / (R * 2 * 128 * a.nb_gu * 8), a.cost_gu);
+        pl.S_d = pick_split((long long) J * a.nb_d, a.kq_d, a.grid_ctas, a.part_bytes / (R * 128 * a.nb_d * 8), a.cost_d);
         pl.ntok = a.ntok; pl.topk = a.topk; pl.pad = 0;
         pl.next_gu = 0; pl.next_d = 0;
         *a.plan = pl;
@@ -229,7 +227,11 @@ cudaError_t launch_route(const Layer& L, const void* sel, int sel_i64, const voi
     a.maxm = maxm;
     a.sel = sel; a.sel_i64 = sel_i64; a.w = w; a.w_dtype = w_dtype;
     a.ntok = ntok; a.topk = topk; a.E = L.E; a.has_shared = L.has_shared; a.first = L.first;
-    a.nb_gu = L.I / 128; a.nb_d = L.H / 128; a.kq_gu = L.H / 128; a.kq_d = L.I / 128;
+    a.nb_gu = L.I / 128; a.nb_d = L.H / 128;
+    // the EXACT GEMV's stages may hold two 128-input blocks; the I16 GEMV's hold one
+    const int hb_gu = maxm == EXACT_MAXM ? exact_stage_blocks(L, 0) : 1, hb_d = maxm == EXACT_MAXM ? exact_stage_blocks(L, 2) : 1;
+    a.kq_gu = L.H / (128 * hb_gu); a.kq_d = L.I / (128 * hb_d);
+    a.cost_gu = 2 / hb_gu; a.cost_d = 2 / hb_d;
     a.grid_ctas = grid_ctas;
     a.part_bytes = (long long) lay.part_bytes;
     a.plan = reinterpret_cast<Plan*>(ws + lay.plan);

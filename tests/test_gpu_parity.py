@@ -127,6 +127,27 @@ def test_exact_layer_mixed_bitrate(oracle, dev, bits):
     assert_exact_mode(got, want, label=str(bits), floor=True)
 
 
+@pytest.mark.parametrize("ntok", [3, 40])
+@pytest.mark.parametrize("H,I,bits", [(640, 384, (3, 3, 3)), (768, 384, (2, 3, 2)), (640, 512, (3, 3, 2)),
+                                      (1024, 512, (3, 3, 4))])
+def test_exact_stage_forms(oracle, dev, H, I, bits, ntok):
+    """The EXACT GEMV streams two 128-input blocks per pipeline stage where its K (H for gate/up, I for down) is a
+    multiple of 256 and its bitrates are at most 3, one block otherwise, and the split plan counts K splits in the
+    same stages. These layers take the one-block form for one or both GEMVs (K an odd number of blocks, or K=4); at
+    40 tokens the plan also splits K. Held to the fixed floors of the EXACT rule: the reference's non-band moe_forward
+    does not serve H=640 (measured 3.8 x RMS from the restatement there), so it sets no bar."""
+    from glmx import synth
+    E = 6
+    bank = synth.make_bank(H, I, E, shared=True, bits=bits, seed=H + I + ntok)
+    layer = _layer(bank, dev)
+    x = synth.make_x(ntok, H, 73 + ntok)
+    sel, w = synth.route_uniform(ntok, E, 4, 83 + ntok)
+    got = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(sel).to(dev), torch.from_numpy(w).to(dev),
+                        mode=1).cpu().numpy()
+    want = oracle.moe_forward(bank, x.astype(np.float32), sel, w, mode=1)
+    assert_exact_mode(got, want, label=f"H={H} I={I} {bits} ntok={ntok}", floor=True)
+
+
 def test_accumulate_and_fp16_out(oracle, dev):
     from glmx import synth
     E = 8
