@@ -177,8 +177,8 @@ __device__ __forceinline__ void item_consume_tc(uint8_t* ring, uint64_t* full, u
 }
 
 // EXACT-mode GEMV (one persistent kernel per phase). Items (job of <= 8 rows, 128-column block, K split); per item the
-// producer warp's lane 0 streams the stages (trellis: one 2-D tensor copy per stage; activations: one bulk copy per
-// row), the 8 consumer warps decode (byte sums on the integer tensor pipe, codebook by HFMA2) and form each 16x16 tile's
+// producer warp's lane 0 streams the stages of HB 128-input blocks (trellis: one 2-D tensor copy per block;
+// activations: one bulk copy per row), the 8 consumer warps decode (byte sums on the integer tensor pipe, codebook by HFMA2) and form each 16x16 tile's
 // products with m16n8k16 MMAs against the job's 8 token columns in chains of TCHAIN tiles started from zero
 // (stage_tc); the chain sums are added on the CUDA cores, block sums compensated (Fast2Sum, TwoSum across K splits).
 template <int K0, int K1, int NMAT, bool GATEUP, int HB>
